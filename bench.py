@@ -1,0 +1,508 @@
+"""Decode-step benchmark: tokens/s and HBM GB/s of RoPE + KV-cache write +
+paged attention over a ragged batch (Qwen2.5-3B-shaped: 64 sequences with
+context U[128, 4096], 16 query / 2 KV heads, head_dim 128, block_size 16,
+40k-block pool, bf16, RoPE theta 1e6), on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decode step of one attention layer: the fused RoPE + cache
+write kernel, then the paged-attention kernel, for every sequence of the
+batch. Steps rotate over independent layers (own KV pool, tables, inputs), so
+consecutive steps never find their KV in L2. With N GPUs (torchrun, one
+process per GPU) the global batch is 64*N sequences drawn from the same
+distribution and assigned to GPUs by LPT on context length; each GPU owns its
+pool and metadata and no collective touches the data path (weak scaling).
+
+Printed (rank 0, one JSON line): value = whole-job tokens/s from CUDA events
+over the timed region (max over ranks), e2e = the same through the public op
+API with inputs copied from pinned host memory every step and the output
+read back, roofline of the attention kernel, the CPU oracle timed on this
+host, clocks sampled during the timed region.
+
+``--impl reference`` times the reference algorithm on the host cores (the
+CPU oracle: the reference has no CPU kernels of its own for this path) on
+bounded samples of the same workload, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "tinyllama.py_b200"))
+sys.path.insert(0, str(REPO))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "decode-attention tokens/sec and HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+UNIT = "tokens/s"
+WORKLOAD = "qwen2.5-3b decode step: 64 seqs/GPU, ctx U[128,4096], 16q/2kv heads, hd128, bs16, bf16"
+LAYERS = 4           # rotating independent KV pools
+FALLBACK_HBM_GBS = 6650.0
+NOMINAL_HBM_GBS = 8000.0
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU-baseline sample budget (rank 0, N=1)")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ setup
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def global_lengths(n_gpus: int, seed: int):
+    from paged_decode import workloads as W
+
+    return W.qwen3b_decode(seed, batch=64 * n_gpus).seq_lens
+
+
+def rank_spec(rank: int, world: int, seed: int, layer: int):
+    from paged_decode import partition as P
+    from paged_decode import workloads as W
+
+    lens = global_lengths(world, seed)
+    shard = P.lpt_assign(lens, world)[rank]
+    base = W.qwen3b_decode(seed)
+    return W.DecodeSpec(base.name, [lens[i] for i in shard], base.num_heads, base.num_kv_heads,
+                        base.head_dim, base.block_size, base.dtype, num_blocks=base.num_blocks,
+                        rope_theta=base.rope_theta, max_position=base.max_position,
+                        seed=seed * 1000 + rank * 10 + layer)
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices):
+        self.devices = devices
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if visible:
+            ids = [v.strip() for v in visible.split(",") if v.strip()]
+            sel = ",".join(ids[d] for d in self.devices if d < len(ids))
+        else:
+            sel = ",".join(map(str, self.devices))
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", sel],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=2)
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- ours
+def measured_hbm_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(key: str):
+    """DRAM bytes per attention launch from the committed ncu summary, if any."""
+    p = REPO / "profiles" / "roofline_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith(key + "="):
+            try:
+                return float(line.split("=", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def run_ours(args, rank, world, local):
+    import torch.distributed as dist
+
+    from cscr import attention as A
+    from cscr import pos_encoding as PE
+    from oracle import decode_oracle as O
+    from paged_decode import workloads as W
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=300))
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    layers = [W.make_batch(rank_spec(rank, world, args.seed, l), device=dev) for l in range(LAYERS)]
+    spec0 = layers[0].spec
+    S, H, KVH, D = len(spec0.seq_lens), spec0.num_heads, spec0.num_kv_heads, spec0.head_dim
+    stream = torch.cuda.Stream(dev)
+
+    def step(b):
+        q2 = b.query.view(S, H * D)
+        k2 = b.key.view(S, KVH * D)
+        q_rot = PE.rotary_embedding_neox_with_cache(b.positions, q2, k2, b.value, b.key_cache,
+                                                    b.value_cache, b.slot_mapping, D,
+                                                    b.cos_sin_cache)
+        return A.paged_attention(q_rot.view(S, H, D), b.key_cache, b.value_cache,
+                                 b.block_tables, b.seq_lens, b.scale)
+
+    def attn_only(b):
+        return A.paged_attention(b.query, b.key_cache, b.value_cache, b.block_tables,
+                                 b.seq_lens, b.scale)
+
+    with torch.cuda.stream(stream):
+        for b in layers:  # warm: workspace, attributes, tensor maps
+            step(b)
+            attn_only(b)
+        stream.synchronize()
+        g_step, g_attn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step, stream=stream):
+            for b in layers:
+                step(b)
+        with torch.cuda.graph(g_attn, stream=stream):
+            for b in layers:
+                attn_only(b)
+
+    reps = max(1, args.steps // LAYERS)
+    steps = reps * LAYERS
+    wreps = max(1, math.ceil(args.warmup / LAYERS))
+
+    def timed(graph, n):
+        with torch.cuda.stream(stream):
+            for _ in range(wreps):
+                graph.replay()
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(n):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    devices = list(range(world)) if world > 1 else [local]
+    sampler = ClockSampler(devices) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    step_ms = timed(g_step, reps)
+    if sampler:
+        sampler.__exit__(None, None, None)
+    attn_ms = timed(g_attn, reps)
+
+    # ---- end to end through the public ops, host buffers each step
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, layers, step, stream, dev, world, barrier, rank)
+
+    tokens_per_step = 64 * world
+    value = tokens_per_step * steps / (step_ms / 1e3)
+    lens_all = [b.seq_lens.cpu().numpy() for b in layers]
+    attn_bytes = statistics.fmean(
+        O.attention_bytes(l, spec0.block_size, H, KVH, D, 2) for l in lens_all)
+    rope_bytes = O.rope_bytes(S, H, KVH, D, D, 2) + O.cache_write_bytes(S, KVH, D, 2)
+    t_attn_us = attn_ms * 1e3 / steps
+    t_step_us = step_ms * 1e3 / steps
+    achieved = attn_bytes / (t_attn_us * 1e-6) / 1e9
+    peak, peak_kind = measured_hbm_peak()
+    traffic = profiled_traffic("qwen3b_decode_attention_bytes_per_launch")
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": wreps * LAYERS, "ms_per_step": round(step_ms / steps, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v and KV pool, seeded lengths)",
+        "config": {"workload": WORKLOAD, "global_batch": tokens_per_step, "seq_len": "U[128,4096]",
+                   "parallelism": f"sequence-sharded x{world} (LPT), no collective",
+                   "l2": f"{LAYERS} rotating independent KV pools per GPU "
+                         f"(~{LAYERS * attn_bytes / 1e6:.0f} MB of KV per rotation > 126 MB L2)",
+                   "timed_region": "CUDA-graph replay of fused RoPE+cache-write + paged attention"},
+        "hbm_gbs_step": round((attn_bytes + rope_bytes) / (t_step_us * 1e-6) / 1e9, 1),
+        "hbm_frac_of_8tbs_step": round((attn_bytes + rope_bytes) / (t_step_us * 1e-6) / 1e9
+                                       / NOMINAL_HBM_GBS, 4),
+        "roofline": {"kernel": "paged_attention_tc_kernel", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                     "algorithmic_bytes_per_launch": int(attn_bytes),
+                     "launch_us": round(t_attn_us, 3),
+                     "traffic": traffic},
+        "gpu_launches": 2 * steps * world,
+        "gpu_launches_per_rank": 2 * steps,
+        "clocks": sampler.summary() if sampler else None,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(layers[0], args.cpu_seconds)
+    return line
+
+
+def pack_layout(S, H, KVH, D, maxB):
+    """Byte offsets of one step's inputs in a single host/device buffer."""
+    segs = [("query", S * H * D * 2), ("key", S * KVH * D * 2), ("value", S * KVH * D * 2),
+            ("positions", S * 8), ("slots", S * 8), ("tables", S * maxB * 4), ("lens", S * 4)]
+    off, out = 0, {}
+    for name, n in segs:
+        out[name] = (off, n)
+        off += (n + 255) // 256 * 256
+    return out, off
+
+
+def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
+    """Same steps through the op API with pinned-host inputs and a host read-back."""
+    import torch.distributed as dist
+
+    from cscr import attention as A
+    from cscr import pos_encoding as PE
+
+    spec0 = layers[0].spec
+    S, H, KVH, D = len(spec0.seq_lens), spec0.num_heads, spec0.num_kv_heads, spec0.head_dim
+    maxB = max(b.block_tables.shape[1] for b in layers)
+    layout, total = pack_layout(S, H, KVH, D, maxB)
+    hosts, devs, views, outs = [], [], [], []
+    for b in layers:
+        h = torch.zeros(total, dtype=torch.uint8).pin_memory()
+
+        def put(name, t):
+            o, n = layout[name]
+            h[o:o + n].copy_(t.contiguous().view(torch.uint8).view(-1).cpu())
+
+        bt = torch.zeros(S, maxB, dtype=torch.int32)
+        bt[:, : b.block_tables.shape[1]] = b.block_tables.cpu()
+        put("query", b.query); put("key", b.key); put("value", b.value)
+        put("positions", b.positions); put("slots", b.slot_mapping)
+        put("tables", bt); put("lens", b.seq_lens)
+        d = torch.empty(total, dtype=torch.uint8, device=dev)
+
+        def view(name, dtype, shape):
+            o, n = layout[name]
+            return d[o:o + n].view(dtype).view(*shape)
+
+        v = dict(query=view("query", torch.bfloat16, (S, H * D)),
+                 key=view("key", torch.bfloat16, (S, KVH * D)),
+                 value=view("value", torch.bfloat16, (S, KVH, D)),
+                 positions=view("positions", torch.int64, (S,)),
+                 slots=view("slots", torch.int64, (S,)),
+                 tables=view("tables", torch.int32, (S, maxB)),
+                 lens=view("lens", torch.int32, (S,)))
+        hosts.append(h); devs.append(d); views.append(v)
+        outs.append(torch.empty(S, H, D, dtype=torch.bfloat16).pin_memory())
+
+    def one(i):
+        r = i % LAYERS
+        b, v = layers[r], views[r]
+        devs[r].copy_(hosts[r], non_blocking=True)
+        q_rot = PE.rotary_embedding_neox_with_cache(v["positions"], v["query"], v["key"],
+                                                    v["value"], b.key_cache, b.value_cache,
+                                                    v["slots"], D, b.cos_sin_cache)
+        out = A.paged_attention(q_rot.view(S, H, D), b.key_cache, b.value_cache, v["tables"],
+                                v["lens"], b.scale)
+        outs[r].copy_(out, non_blocking=True)
+
+    steps = max(LAYERS, (args.steps // 4) // LAYERS * LAYERS)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, LAYERS)):
+            one(i)
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            one(i)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return {"value": round(64 * world * steps / (ms / 1e3), 1), "unit": UNIT,
+            "h2d_bytes_per_step": int(total), "d2h_bytes_per_step": int(S * H * D * 2),
+            "steps": steps,
+            "path": "cscr.pos_encoding.rotary_embedding_neox_with_cache + "
+                    "cscr.attention.paged_attention, one pinned H2D + one D2H per step"}
+
+
+# ------------------------------------------------------------ CPU side
+def oracle_inputs(batch):
+    """Host copies of one layer's decode step, pool cut to the blocks it uses."""
+    from paged_decode import workloads as W
+
+    kc, vc, tables, lens = W.compact_for_oracle(batch)
+    S = batch.num_decode
+    pos = batch.positions.cpu().numpy()
+    # the new token's slot, renumbered into the compacted pool
+    bs = batch.spec.block_size
+    slots = np.array([tables[s, pos[s] // bs] * bs + pos[s] % bs for s in range(S)], np.int64)
+    return dict(q=W.to_numpy(batch.query.view(S, -1)), k=W.to_numpy(batch.key.view(S, -1)),
+                v=W.to_numpy(batch.value), pos=pos, slots=slots, tables=tables, lens=lens,
+                kc=kc, vc=vc, cs=W.to_numpy(batch.cos_sin_cache), scale=batch.scale,
+                H=batch.spec.num_heads, D=batch.spec.head_dim)
+
+
+def oracle_step(inp, seqs, threads):
+    """The reference algorithm for a subset of sequences: RoPE, KV write, attention."""
+    from oracle import decode_oracle as O
+
+    idx = np.asarray(seqs)
+    q_rot, k_rot = O.rotary_embedding_neox(inp["pos"][idx], inp["q"][idx], inp["k"][idx],
+                                           inp["D"], inp["cs"], "bfloat16")
+    O.reshape_and_cache(k_rot, inp["v"][idx], inp["kc"], inp["vc"], inp["slots"][idx])
+    return O.paged_attention_threads(q_rot.reshape(len(idx), inp["H"], inp["D"]), inp["kc"],
+                                     inp["vc"], inp["tables"][idx], inp["lens"][idx],
+                                     inp["scale"], "bfloat16", threads)
+
+
+def cpu_baseline(batch, seconds):
+    cores = os.cpu_count() or 1
+    inp = oracle_inputs(batch)
+    S = len(inp["lens"])
+    chunk = min(S, cores)
+    done, t0, i = 0, time.perf_counter(), 0
+    while True:
+        seqs = [(i * chunk + j) % S for j in range(chunk)]
+        oracle_step(inp, seqs, cores)
+        done += chunk
+        i += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and done >= S:
+            break
+    return {"value": round(done / el, 2), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"CPU oracle (numpy, {cores} threads) over {done} sequences of the same "
+                      f"workload in chunks of {chunk}, {el:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from paged_decode import workloads as W
+
+    batch = W.make_batch(rank_spec(0, 1, args.seed, 0), device="cpu")
+    inp = oracle_inputs(batch)
+    cores = os.cpu_count() or 1
+    S = len(inp["lens"])
+    chunk = min(S, cores)
+    for i in range(args.warmup):
+        oracle_step(inp, [(i * chunk + j) % S for j in range(chunk)], cores)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        oracle_step(inp, [(i * chunk + j) % S for j in range(chunk)], cores)
+    el = time.perf_counter() - t0
+    value = chunk * args.steps / el
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v and KV pool, seeded lengths)",
+        "config": {"workload": WORKLOAD, "global_batch": 64,
+                   "sample_per_step": f"{chunk} of the 64 sequences (rotating)"},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"each step: RoPE + cache write + attention of {chunk} "
+                                   f"sequences, CPU oracle (numpy, {cores} threads)"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        print(json.dumps({"error": "launch with torchrun for --gpus > 1"}))
+        sys.exit(2)
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        line = run_ours(args, rank, world, local)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,241 @@
+/*
+ * tinyllama_b200.h — C ABI of the B200 (sm_100a) decode hot path.
+ *
+ * One shared library, libtinyllama_b200.so, exports every entry point below.
+ * The signatures carry only plain pointers, sizes and enums: no torch or
+ * pybind types cross this boundary, so the Python op modules (cscr.attention,
+ * cscr.cache, cscr.pos_encoding), a ctypes/cffi binding or a C++ engine can
+ * all bind it the same way.
+ *
+ * Conventions shared by every entry point
+ *   - Device pointers belong to the device that is current on the calling
+ *     thread; the caller selects it (cudaSetDevice / a device guard) first.
+ *   - `stream` is a cudaStream_t passed as void*. NULL means the legacy
+ *     default stream. All work is enqueued asynchronously on that stream;
+ *     nothing synchronises the host.
+ *   - The return value is a tlb_status. On failure tlb_last_error() returns
+ *     a message for the calling thread (valid until its next call).
+ *   - Element types are given by tlb_dtype. All tensors are dense row-major
+ *     ("contiguous" in torch terms) unless a stride argument says otherwise.
+ *   - Kernels never trap: inputs that the reference would read out of
+ *     bounds (a block id outside the pool, a position beyond the cos/sin
+ *     table, a slot outside the cache) are skipped and a bit is set in a
+ *     per-device status word, readable with tlb_get_device_status().
+ */
+#ifndef TINYLLAMA_B200_H_
+#define TINYLLAMA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TLB_API __attribute__((visibility("default")))
+#else
+#define TLB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tlb_status {
+    TLB_OK = 0,
+    TLB_ERR_INVALID_ARGUMENT = 1, /* shape / dtype / alignment check failed */
+    TLB_ERR_UNSUPPORTED = 2,      /* valid request this build cannot serve */
+    TLB_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
+    TLB_ERR_WORKSPACE = 4         /* workspace missing or too small */
+} tlb_status;
+
+typedef enum tlb_dtype {
+    TLB_FLOAT32 = 0,
+    TLB_FLOAT16 = 1,
+    TLB_BFLOAT16 = 2,
+    TLB_INT32 = 3,
+    TLB_INT64 = 4
+} tlb_dtype;
+
+/* Bits of the per-device status word (tlb_get_device_status). */
+#define TLB_STATUS_BAD_BLOCK_ID     0x1u  /* block id >= num_blocks in a block table */
+#define TLB_STATUS_SEQ_TOO_LONG     0x2u  /* seq_len > max_blocks_per_seq * block_size */
+#define TLB_STATUS_BAD_POSITION     0x4u  /* RoPE position outside the cos/sin table */
+#define TLB_STATUS_BAD_SLOT         0x8u  /* slot / logical block outside the cache */
+#define TLB_STATUS_WAIT_TIMEOUT     0x10u /* a bounded pipeline wait gave up */
+
+/* Message describing the last failure on the calling thread ("" if none). */
+TLB_API const char* tlb_last_error(void);
+
+/* Library version string. */
+TLB_API const char* tlb_version(void);
+
+/* Reads (and, if clear != 0, resets) the status word of the current device.
+ * Enqueued on `stream` and waits for it: a debugging aid, not a hot-path
+ * call. */
+TLB_API int tlb_get_device_status(uint32_t* status_out, int clear, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged attention (decode: one query token per sequence).
+ *
+ * Replaces the pybind op `paged_attention(query, key_cache, value_cache,
+ * block_tables, seq_lens, scale)` of cscr/attention.cpp:7-48 and its kernel
+ * launch cscr/attention_kernel.cu:111-150.
+ *
+ *   out, query   : [num_seqs, num_heads, head_dim]            dtype
+ *   key_cache    : [num_blocks, num_kv_heads, block_size, head_dim]  dtype
+ *   value_cache  : same shape as key_cache                     dtype
+ *   block_tables : [num_seqs, max_blocks_per_seq] int32 (entries < 0 skipped)
+ *   seq_lens     : [num_seqs] int32
+ *   dtype        : TLB_FLOAT32, TLB_FLOAT16 or TLB_BFLOAT16
+ *
+ * Query head h attends to KV head h / (num_heads / num_kv_heads). A sequence
+ * whose length is <= 0, or whose blocks are all skipped, yields zeros.
+ *
+ * `workspace` is device scratch of at least the size that
+ * tlb_paged_attention_workspace_size() returns for the same arguments. Its
+ * first tlb_paged_attention_workspace_zeroed_bytes() bytes must be zero
+ * before the first call; every call leaves them zero again, so one
+ * zero-initialised buffer can be reused by successive calls on one stream.
+ * Calls that overlap in time must use different workspaces.
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_paged_attention_workspace_size(int64_t num_seqs, int64_t num_heads,
+                                       int64_t num_kv_heads, int64_t head_dim,
+                                       int dtype, size_t* bytes_out);
+
+TLB_API int tlb_paged_attention_workspace_zeroed_bytes(int64_t num_seqs,
+                                               int64_t num_kv_heads,
+                                               size_t* bytes_out);
+
+TLB_API int tlb_paged_attention(void* out, const void* query, const void* key_cache,
+                        const void* value_cache, const int32_t* block_tables,
+                        const int32_t* seq_lens, int64_t num_seqs,
+                        int64_t num_heads, int64_t num_kv_heads,
+                        int64_t head_dim, int64_t num_blocks,
+                        int64_t block_size, int64_t max_blocks_per_seq,
+                        float scale, int dtype, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * NeoX rotary embedding.
+ *
+ * Replaces `rotary_embedding_neox(postions, query, key, head_size,
+ * cos_sin_cache)` of cscr/pos_encoding.cpp:7-18 and the launch
+ * cscr/pos_encoding_kernel.cu:70-134.
+ *
+ *   positions     : [num_tokens] of pos_dtype (TLB_INT32 or TLB_INT64)
+ *   query         : [num_tokens, num_heads * head_size]; row stride query_stride
+ *   key           : [num_tokens, num_kv_heads * head_size]; rotated IN PLACE
+ *   out           : [num_tokens, num_heads * head_size]; rotated query
+ *   cos_sin_cache : [cache_rows, rot_dim]; cos in [:rot_dim/2], sin after
+ *
+ * Pairs (i, i + rot_dim/2), i < rot_dim/2, of each head are rotated:
+ * x' = x cos - y sin, y' = y cos + x sin, in fp32, rounded once to dtype.
+ * Query elements at and beyond rot_dim are copied to `out` unchanged.
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_rotary_embedding_neox(void* out, const void* positions, int pos_dtype,
+                              const void* query, void* key, int64_t num_tokens,
+                              int64_t num_heads, int64_t num_kv_heads,
+                              int64_t head_size, const void* cos_sin_cache,
+                              int64_t cache_rows, int64_t rot_dim,
+                              int64_t query_stride, int64_t key_stride,
+                              int64_t out_stride, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * KV-cache write ("reshape_and_cache").
+ *
+ * The reference writes new keys/values with torch advanced indexing in
+ * PagedAttentionWithRoPE._write_kv_cache (src/model_executor/layers/
+ * attention.py:82-116); it has no native op. This entry point is that step
+ * as one kernel, addressed by a slot mapping:
+ *
+ *   key, value  : [num_tokens, num_kv_heads, head_size]; row strides
+ *                 key_stride / value_stride (elements between tokens)
+ *   key_cache, value_cache : [num_blocks, num_kv_heads, block_size, head_size]
+ *   slots       : [num_tokens] of slot_dtype (TLB_INT32 or TLB_INT64);
+ *                 slot = block * block_size + offset; slot < 0 skips the token
+ *
+ * Bit-exact copy; tokens whose slot is outside the cache are skipped and
+ * flagged (TLB_STATUS_BAD_SLOT).
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_reshape_and_cache(const void* key, const void* value, void* key_cache,
+                          void* value_cache, const void* slots, int slot_dtype,
+                          int64_t num_tokens, int64_t num_kv_heads,
+                          int64_t head_size, int64_t num_blocks,
+                          int64_t block_size, int64_t key_stride,
+                          int64_t value_stride, int dtype, void* stream);
+
+/* The same write addressed exactly as _write_kv_cache addresses it
+ * (attention.py:96-116): token r goes to block
+ * block_tables[r, positions[r] / block_size], offset positions[r] %
+ * block_size, and is skipped when that block id is negative. No host sync. */
+TLB_API int tlb_write_kv_cache(const void* key, const void* value, void* key_cache,
+                       void* value_cache, const void* positions, int pos_dtype,
+                       const int32_t* block_tables, int64_t max_blocks_per_seq,
+                       int64_t num_tokens, int64_t num_kv_heads,
+                       int64_t head_size, int64_t num_blocks,
+                       int64_t block_size, int64_t key_stride,
+                       int64_t value_stride, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused NeoX RoPE + KV-cache write: one launch that does
+ * tlb_rotary_embedding_neox (query -> out, key rotated in place) and then
+ * writes the rotated key and `value` into the caches, without reading the
+ * rotated key back. Same argument meaning as the calls it replaces
+ * (pos_encoding_kernel.cu:24-65 followed by attention.py:96-116).
+ * The destination comes from `slots` (as tlb_reshape_and_cache) when it is
+ * non-null, otherwise from block_tables/positions (as tlb_write_kv_cache,
+ * block_tables [num_tokens, max_blocks_per_seq] int32).
+ * `value_stride` is in elements between tokens; key rows use key_stride.
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_rotary_embedding_neox_with_cache(
+    void* out, const void* positions, int pos_dtype, const void* query,
+    void* key, const void* value, void* key_cache, void* value_cache,
+    const void* slots, int slot_dtype, const int32_t* block_tables,
+    int64_t max_blocks_per_seq, int64_t num_tokens, int64_t num_heads,
+    int64_t num_kv_heads, int64_t head_size, const void* cos_sin_cache,
+    int64_t cache_rows, int64_t rot_dim, int64_t num_blocks,
+    int64_t block_size, int64_t query_stride, int64_t key_stride,
+    int64_t value_stride, int64_t out_stride, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Block copies (cscr/cache.cpp:94-151, cscr/cache_kernel.cu:124-212).
+ *
+ * `pairs` is HOST memory: num_pairs (src_block, dst_block) int64 pairs.
+ * A block is `block_bytes` contiguous bytes; block b of a cache starts at
+ * base + b * block_bytes.
+ *
+ * tlb_copy_blocks copies, inside each of the `num_caches` device caches
+ * listed in `caches` (host array of device pointers: every layer's key and
+ * value cache), block src -> dst for every pair, in ONE launch.
+ *
+ * tlb_swap_blocks copies block src of `src` to block dst of `dst`;
+ * src_on_device / dst_on_device say where each lives (1 = current device,
+ * 0 = host memory). Device<->device uses a kernel, host<->device one
+ * cudaMemcpyAsync per run of consecutive blocks, host<->host memcpy.
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_copy_blocks(void* const* caches, int64_t num_caches,
+                    const int64_t* pairs, int64_t num_pairs,
+                    int64_t block_bytes, void* stream);
+
+TLB_API int tlb_swap_blocks(const void* src, int src_on_device, void* dst,
+                    int dst_on_device, const int64_t* pairs, int64_t num_pairs,
+                    int64_t block_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Decode metadata on the device (src/worker/worker.py:139-159): for each
+ * decode sequence r, position = context_len - 1 and
+ * slot = block_tables[r, position / block_size] * block_size
+ *        + position % block_size
+ * (-1 when the context is empty or the block id is negative).
+ *   context_lens : [num_seqs] int32; block_tables [num_seqs, max_blocks] int32
+ *   positions_out: [num_seqs] int64; slots_out: [num_seqs] int64
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_decode_metadata(const int32_t* context_lens,
+                        const int32_t* block_tables, int64_t num_seqs,
+                        int64_t max_blocks_per_seq, int64_t block_size,
+                        int64_t* positions_out, int64_t* slots_out,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TINYLLAMA_B200_H_ */

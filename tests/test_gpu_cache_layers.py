@@ -1,0 +1,109 @@
+"""Block copies, device-side metadata and the layer glue on the GPU."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from cscr import _lib
+from cscr import cache as C
+from helpers import check_attention, tol_for
+from oracle import decode_oracle as O
+from paged_decode import metadata as M
+from paged_decode import workloads as W
+from paged_decode.layers import PagedAttentionWithRoPE
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _dev():
+    torch.cuda.set_device(0)
+    yield
+    torch.cuda.synchronize()
+
+
+def test_copy_blocks_all_layers_one_launch(built_lib):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    layers = 5
+    kcs = [torch.randn(64, 2, 16, 128, generator=g, device="cuda").to(torch.bfloat16)
+           for _ in range(layers)]
+    vcs = [torch.randn(64, 2, 16, 128, generator=g, device="cuda").to(torch.bfloat16)
+           for _ in range(layers)]
+    mapping = {3: [10, 11], 7: [40], 0: [63, 1, 2]}
+    ref = [W.to_numpy(c) for c in kcs + vcs]
+    O.copy_blocks(ref, mapping)
+    C.copy_blocks(kcs, vcs, mapping)
+    for got, r in zip(kcs + vcs, ref):
+        assert np.array_equal(W.to_numpy(got), r)
+
+
+@pytest.mark.parametrize("direction", ["d2d", "d2h", "h2d", "h2h"])
+def test_swap_blocks(direction, built_lib):
+    g = torch.Generator().manual_seed(1)
+    src = torch.randn(32, 2, 8, 64, generator=g).to(torch.float16)
+    dst = torch.randn(48, 2, 8, 64, generator=g).to(torch.float16)
+    mapping = {1: 5, 2: 6, 3: 7, 30: 0, 9: 47}
+    ref = W.to_numpy(dst).copy()
+    O.swap_blocks(W.to_numpy(src), ref, mapping)
+    if direction[0] == "d":
+        src = src.cuda()
+    if direction[2] == "d":
+        dst = dst.cuda()
+    C.swap_blocks(src, dst, mapping)
+    torch.cuda.synchronize()
+    assert np.array_equal(W.to_numpy(dst), ref)
+
+
+def test_copy_blocks_reference_errors():
+    with pytest.raises(RuntimeError, match="same number of layers"):
+        C.copy_blocks([torch.zeros(2, 2)], [], {0: [1]})
+    with pytest.raises(RuntimeError, match="cache tensors must be CUDA tensors"):
+        C.copy_blocks([torch.zeros(2, 2)], [torch.zeros(2, 2)], {0: [1]})
+
+
+def test_decode_metadata_matches_reference_worker(built_lib):
+    z = np.load(GOLDEN / "decode_meta.npz")
+    tables = [row[row >= 0].tolist() for row in z["block_tables"]]
+    md = M.decode_metadata(tables, z["context_lens"].tolist(), int(z["block_size"]))
+    assert np.array_equal(md.positions.cpu().numpy(), z["positions"])
+    assert np.array_equal(md.slot_mapping.cpu().numpy(), z["slots"])
+    assert np.array_equal(md.context_lens.cpu().numpy(), z["context_lens"])
+
+
+@pytest.mark.parametrize("build", [torch.float32, torch.bfloat16])
+def test_paged_attention_with_rope_layer(build, built_lib):
+    """Reference layer forward: RoPE -> _write_kv_cache -> attention, on the fused ops."""
+    spec = W.DecodeSpec("layer", [1, 17, 64, 300, 2048, 4096, 33, 1000], 16, 2, 128, 16,
+                        "bfloat16", num_blocks=2048, rope_theta=1e6, max_position=4096)
+    b = W.make_batch(spec)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(build)
+    try:
+        layer = PagedAttentionWithRoPE(16, 128, 128 ** -0.5, 128, max_position=4096,
+                                       base=1_000_000).cuda()
+    finally:
+        torch.set_default_dtype(prev)
+    S = b.num_decode
+    cs = layer.cos_sin_cache.to(torch.bfloat16)
+    # oracle pipeline on host copies
+    q_np = W.to_numpy(b.query.reshape(S, -1))
+    k_np = W.to_numpy(b.key.reshape(S, -1))
+    q_rot, k_rot = O.rotary_embedding_neox(W.to_numpy(b.positions), q_np, k_np, 128,
+                                           W.to_numpy(cs), "bfloat16")
+    kc, vc = W.to_numpy(b.key_cache), W.to_numpy(b.value_cache)
+    out = layer(b.positions, b.query, b.key, b.value, b.key_cache, b.value_cache,
+                b.block_tables, b.seq_lens)
+    # the layer rotated `key` in place (as the reference does) ...
+    k_dev = W.to_numpy(b.key.reshape(S, -1))
+    np.testing.assert_allclose(O.to_f32(k_dev, "bfloat16"), O.to_f32(k_rot, "bfloat16"),
+                               **tol_for("bfloat16"))
+    # ... and wrote exactly that key and the value where _write_kv_cache would
+    O.write_kv_cache(k_dev, W.to_numpy(b.value), W.to_numpy(b.positions), kc, vc,
+                     W.to_numpy(b.block_tables))
+    assert np.array_equal(W.to_numpy(b.key_cache), kc)
+    assert np.array_equal(W.to_numpy(b.value_cache), vc)
+    ref = O.paged_attention(q_rot.reshape(S, 16, 128), kc, vc, W.to_numpy(b.block_tables),
+                            W.to_numpy(b.seq_lens), b.scale, "bfloat16")
+    np.testing.assert_allclose(O.to_f32(W.to_numpy(out), "bfloat16"), O.to_f32(ref, "bfloat16"),
+                               atol=1e-2, rtol=2e-2)

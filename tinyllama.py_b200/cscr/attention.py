@@ -1,0 +1,115 @@
+"""cscr.attention — drop-in for the reference's pybind module of the same name.
+
+``paged_attention(query, key_cache, value_cache, block_tables, seq_lens, scale)``
+keeps the signature, keyword names, checks and error messages of
+cscr/attention.cpp:7-48 (bound at :50-56) and returns a new
+``[num_seqs, num_heads, head_dim]`` tensor, computed asynchronously on the
+current CUDA stream by the sm_100a kernels of libtinyllama_b200.so.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import DTYPE_CODE, torch_check
+
+_FLOAT_TYPES = (torch.float16, torch.bfloat16, torch.float32)
+
+# (device index, stream handle) -> zero-initialised uint8 workspace tensor.
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_ws_sizes: dict[tuple, int] = {}
+
+
+def workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                    dtype: torch.dtype, device_index: int) -> int:
+    """Bytes of scratch the attention kernel needs for this shape on this device."""
+    key = (num_seqs, num_heads, num_kv_heads, head_dim, dtype, device_index)
+    n = _ws_sizes.get(key)
+    if n is None:
+        out = ctypes.c_size_t(0)
+        _lib.check(_lib.load().tlb_paged_attention_workspace_size(
+            num_seqs, num_heads, num_kv_heads, head_dim, DTYPE_CODE[dtype], ctypes.byref(out)))
+        n = out.value
+        _ws_sizes[key] = n
+    return n
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    key = (device.index, stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        # Zeroed once: the kernel leaves its arrival counters at zero again.
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def paged_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                    block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                    scale: float) -> torch.Tensor:
+    """PagedAttention decode forward (CUDA, sm_100a).
+
+    query [num_seqs, num_heads, head_dim]; key_cache / value_cache
+    [num_blocks, num_kv_heads, block_size, head_dim]; block_tables
+    [num_seqs, max_blocks_per_seq] int32; seq_lens [num_seqs] int32.
+    """
+    torch_check(query.is_cuda, "query must be a CUDA tensor")
+    torch_check(key_cache.is_cuda, "key_cache must be a CUDA tensor")
+    torch_check(value_cache.is_cuda, "value_cache must be a CUDA tensor")
+    torch_check(block_tables.is_cuda, "block_tables must be a CUDA tensor")
+    torch_check(seq_lens.is_cuda, "seq_lens must be a CUDA tensor")
+    torch_check(query.dim() == 3, "query must be [num_seqs, num_heads, head_dim]")
+    torch_check(key_cache.dim() == 4,
+                "key_cache must be [num_blocks, num_kv_heads, block_size, head_dim]")
+    torch_check(value_cache.shape == key_cache.shape,
+                "value_cache must have the same shape as key_cache")
+    torch_check(block_tables.dim() == 2, "block_tables must be [num_seqs, max_blocks_per_seq]")
+    torch_check(seq_lens.dim() == 1, "seq_lens must be [num_seqs]")
+    torch_check(query.is_contiguous(), "query must be contiguous")
+    torch_check(key_cache.is_contiguous(), "key_cache must be contiguous")
+    torch_check(value_cache.is_contiguous(), "value_cache must be contiguous")
+    torch_check(block_tables.is_contiguous(), "block_tables must be contiguous")
+    torch_check(seq_lens.is_contiguous(), "seq_lens must be contiguous")
+    torch_check(block_tables.dtype == torch.int32, "block_tables must be int32")
+    torch_check(seq_lens.dtype == torch.int32, "seq_lens must be int32")
+    torch_check(query.dtype == key_cache.dtype and query.dtype == value_cache.dtype,
+                "query, key_cache and value_cache must share the same dtype")
+    torch_check(query.dtype in _FLOAT_TYPES, "dtype must be float16, bfloat16 or float32")
+
+    num_seqs, num_heads, head_dim = query.shape
+    num_blocks, num_kv_heads, block_size, cache_head_dim = key_cache.shape
+    torch_check(num_seqs > 0, "query must contain at least one sequence")
+    torch_check(head_dim == cache_head_dim, "query head_dim must match the cache head_dim")
+    torch_check(num_heads % num_kv_heads == 0, "num_heads must be divisible by num_kv_heads")
+    torch_check(block_tables.size(0) == num_seqs, "block_tables must have one row per sequence")
+    torch_check(seq_lens.size(0) == num_seqs, "seq_lens must have one entry per sequence")
+    torch_check(head_dim <= 1024, "head_dim too large for the reference kernel")
+    dev = query.device
+    torch_check(key_cache.device == dev and value_cache.device == dev
+                and block_tables.device == dev and seq_lens.device == dev,
+                "all tensors must be on the same CUDA device")
+
+    out = torch.empty_like(query)
+    if num_blocks == 0 or block_tables.size(1) == 0:
+        # No cache to read: every softmax is empty, which the kernel defines as 0.
+        out.zero_()
+        return out
+    lib = _lib.load()
+    with _lib.device_guard(dev):
+        stream = _lib.stream_of(dev)
+        nbytes = workspace_bytes(num_seqs, num_heads, num_kv_heads, head_dim, query.dtype,
+                                 dev.index)
+        ws = _workspace(dev, stream, nbytes)
+        rc = lib.tlb_paged_attention(
+            out.data_ptr(), query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            block_tables.data_ptr(), seq_lens.data_ptr(), num_seqs, num_heads, num_kv_heads,
+            head_dim, num_blocks, block_size, block_tables.size(1), float(scale),
+            DTYPE_CODE[query.dtype], ws.data_ptr() if ws is not None else None,
+            ws.numel() if ws is not None else 0, stream)
+        _lib.check(rc)
+    return out

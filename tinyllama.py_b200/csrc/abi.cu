@@ -1,0 +1,587 @@
+// C ABI of libtinyllama_b200.so: argument checks, path selection, tensor-map
+// encoding and launches. See include/tinyllama_b200.h for the contract.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/tinyllama_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tlb {
+__device__ unsigned int g_status = 0;
+}
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(TLB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define TLB_REQUIRE(cond, ...)                                   \
+    do {                                                         \
+        if (!(cond)) return fail(TLB_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+    } while (0)
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline int elem_bytes(int dtype) {
+    switch (dtype) {
+        case TLB_FLOAT32: return 4;
+        case TLB_FLOAT16: return 2;
+        case TLB_BFLOAT16: return 2;
+        case TLB_INT32: return 4;
+        case TLB_INT64: return 8;
+        default: return 0;
+    }
+}
+inline bool is_float(int dtype) {
+    return dtype == TLB_FLOAT32 || dtype == TLB_FLOAT16 || dtype == TLB_BFLOAT16;
+}
+inline bool is_index(int dtype) { return dtype == TLB_INT32 || dtype == TLB_INT64; }
+
+// ------------------------------------------------------------ tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+struct MapKey {
+    uintptr_t ptr;
+    uint64_t rows;
+    int head_dim;
+    int box_rows;
+    bool operator==(const MapKey& o) const {
+        return ptr == o.ptr && rows == o.rows && head_dim == o.head_dim && box_rows == o.box_rows;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        return std::hash<uintptr_t>()(k.ptr) ^ (std::hash<uint64_t>()(k.rows) * 31u) ^
+               ((size_t)k.head_dim << 20) ^ ((size_t)k.box_rows << 40);
+    }
+};
+
+// A cache viewed as a 2-D tensor [rows = blocks * kv_heads * block_size, head_dim]
+// of 16-bit elements; box = 64 columns (128 bytes, 128-byte swizzle) x block_size rows.
+int kv_tensor_map(const void* base, uint64_t rows, int head_dim, int box_rows, CUtensorMap* out) {
+    static std::mutex mu;
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{reinterpret_cast<uintptr_t>(base), rows, head_dim, box_rows};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return TLB_OK;
+        }
+    }
+    auto fn = encode_fn();
+    if (fn == nullptr) return fail(TLB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TLB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (cache.size() > 4096) cache.clear();
+        cache.emplace(key, m);
+    }
+    *out = m;
+    return TLB_OK;
+}
+
+int current_device(int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    return TLB_OK;
+}
+
+// Workspace layout of the tensor-core attention path.
+struct WsLayout {
+    size_t counters, ml, o, total, zeroed;
+};
+WsLayout ws_layout(int64_t num_seqs, int64_t num_kv_heads, int64_t head_dim, int gpad, int grid) {
+    WsLayout w;
+    w.counters = tlb::attn::kWorkspaceHeader;
+    w.ml = w.counters + align_up((size_t)num_seqs * num_kv_heads * 4, 256);
+    w.zeroed = w.ml;
+    w.o = w.ml + align_up((size_t)2 * grid * gpad * 2 * 4, 256);
+    w.total = w.o + align_up((size_t)2 * grid * gpad * head_dim * 4, 256);
+    return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tlb_last_error(void) { return g_last_error.c_str(); }
+
+const char* tlb_version(void) { return "tinyllama_b200 0.1.0 (sm_100a)"; }
+
+int tlb_get_device_status(uint32_t* status_out, int clear, void* stream) {
+    TLB_REQUIRE(status_out != nullptr, "status_out must not be null");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, tlb::g_status, sizeof(v), 0,
+                                              cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && clear) {
+        static const unsigned int zero = 0;
+        e = cudaMemcpyToSymbolAsync(tlb::g_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice,
+                                    st);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device status word");
+    *status_out = v;
+    return TLB_OK;
+}
+
+// ------------------------------------------------------------ attention
+int tlb_paged_attention_workspace_size(int64_t num_seqs, int64_t num_heads, int64_t num_kv_heads,
+                                       int64_t head_dim, int dtype, size_t* bytes_out) {
+    TLB_REQUIRE(bytes_out != nullptr, "bytes_out must not be null");
+    TLB_REQUIRE(num_seqs > 0 && num_heads > 0 && num_kv_heads > 0 && head_dim > 0,
+                "sizes must be positive");
+    TLB_REQUIRE(num_heads % num_kv_heads == 0, "num_heads must be divisible by num_kv_heads");
+    const int group = (int)(num_heads / num_kv_heads);
+    // Block size does not change the workspace; any supported one answers.
+    if (!tlb::attn::tc_supported(dtype, (int)head_dim, group, 16)) {
+        *bytes_out = 0;
+        return TLB_OK;
+    }
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    cudaError_t e;
+    const int grid = tlb::attn::tc_grid(dev, dtype, (int)head_dim, group, &e);
+    if (grid <= 0) return cuda_fail(e, "sizing the attention grid");
+    *bytes_out = ws_layout(num_seqs, num_kv_heads, head_dim, tlb::attn::tc_gpad(group), grid).total;
+    return TLB_OK;
+}
+
+int tlb_paged_attention_workspace_zeroed_bytes(int64_t num_seqs, int64_t num_kv_heads,
+                                               size_t* bytes_out) {
+    TLB_REQUIRE(bytes_out != nullptr, "bytes_out must not be null");
+    TLB_REQUIRE(num_seqs > 0 && num_kv_heads > 0, "sizes must be positive");
+    *bytes_out = ws_layout(num_seqs, num_kv_heads, 64, 8, 1).zeroed;
+    return TLB_OK;
+}
+
+int tlb_paged_attention(void* out, const void* query, const void* key_cache,
+                        const void* value_cache, const int32_t* block_tables,
+                        const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
+                        int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                        int64_t block_size, int64_t max_blocks_per_seq, float scale, int dtype,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+    TLB_REQUIRE(is_float(dtype), "dtype must be float16, bfloat16 or float32");
+    TLB_REQUIRE(num_seqs > 0, "query must contain at least one sequence");
+    TLB_REQUIRE(num_heads > 0 && num_kv_heads > 0 && head_dim > 0 && num_blocks > 0 &&
+                    block_size > 0 && max_blocks_per_seq > 0,
+                "sizes must be positive");
+    TLB_REQUIRE(num_heads % num_kv_heads == 0, "num_heads must be divisible by num_kv_heads");
+    TLB_REQUIRE(head_dim <= 1024, "head_dim too large for the reference kernel");
+    TLB_REQUIRE(out && query && key_cache && value_cache && block_tables && seq_lens,
+                "tensor pointers must not be null");
+    TLB_REQUIRE(num_seqs < (1ll << 31) && num_heads < (1 << 16) && max_blocks_per_seq < (1ll << 31),
+                "sizes exceed the supported range");
+    const int esz = elem_bytes(dtype);
+    TLB_REQUIRE(aligned(query, esz) && aligned(out, esz) && aligned(key_cache, esz) &&
+                    aligned(value_cache, esz),
+                "tensor pointers must be aligned to the element size");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int group = (int)(num_heads / num_kv_heads);
+    const float scale_log2 = scale * 1.4426950408889634f;
+
+    const uint64_t rows = (uint64_t)num_blocks * num_kv_heads * block_size;
+    const bool tc = tlb::attn::tc_supported(dtype, (int)head_dim, group, (int)block_size) &&
+                    aligned(query, 16) && aligned(key_cache, 16) && aligned(value_cache, 16) &&
+                    rows < (1ull << 31);
+    if (tc) {
+        int dev;
+        if (int rc = current_device(&dev)) return rc;
+        cudaError_t e;
+        const int grid = tlb::attn::tc_grid(dev, dtype, (int)head_dim, group, &e);
+        if (grid <= 0) return cuda_fail(e, "sizing the attention grid");
+        const int gpad = tlb::attn::tc_gpad(group);
+        const WsLayout w = ws_layout(num_seqs, num_kv_heads, head_dim, gpad, grid);
+        if (workspace == nullptr || workspace_bytes < w.total || !aligned(workspace, 256))
+            return fail(TLB_ERR_WORKSPACE,
+                        "paged_attention needs a 256-byte aligned workspace of %zu bytes (got %zu)",
+                        w.total, workspace_bytes);
+        CUtensorMap tk, tv;
+        if (int rc = kv_tensor_map(key_cache, rows, (int)head_dim, (int)block_size, &tk)) return rc;
+        if (int rc = kv_tensor_map(value_cache, rows, (int)head_dim, (int)block_size, &tv)) return rc;
+        tlb::attn::TcParams p;
+        char* ws = static_cast<char*>(workspace);
+        p.out = out;
+        p.query = query;
+        p.block_tables = block_tables;
+        p.seq_lens = seq_lens;
+        p.ws_o = reinterpret_cast<float*>(ws + w.o);
+        p.ws_ml = reinterpret_cast<float*>(ws + w.ml);
+        p.counters = reinterpret_cast<unsigned int*>(ws + w.counters);
+        p.num_blocks = num_blocks;
+        p.num_seqs = (int)num_seqs;
+        p.num_heads = (int)num_heads;
+        p.num_kv_heads = (int)num_kv_heads;
+        p.group = group;
+        p.block_size = (int)block_size;
+        p.max_blocks = (int)max_blocks_per_seq;
+        p.min_units = (int)(512 / block_size) > 0 ? (int)(512 / block_size) : 1;
+        p.scale_log2 = scale_log2;
+        e = tlb::attn::launch_tc(dtype, (int)head_dim, group, p, tk, tv, grid, st);
+        if (e != cudaSuccess) return cuda_fail(e, "launching paged attention");
+        return TLB_OK;
+    }
+    tlb::attn::GenericParams g;
+    g.out = out;
+    g.query = query;
+    g.key_cache = key_cache;
+    g.value_cache = value_cache;
+    g.block_tables = block_tables;
+    g.seq_lens = seq_lens;
+    g.num_blocks = num_blocks;
+    g.num_seqs = (int)num_seqs;
+    g.num_heads = (int)num_heads;
+    g.num_kv_heads = (int)num_kv_heads;
+    g.group = group;
+    g.head_dim = (int)head_dim;
+    g.block_size = (int)block_size;
+    g.max_blocks = (int)max_blocks_per_seq;
+    g.scale_log2 = scale_log2;
+    cudaError_t e = tlb::attn::launch_generic(dtype, g, st);
+    if (e != cudaSuccess) return cuda_fail(e, "launching paged attention");
+    return TLB_OK;
+}
+
+// ---------------------------------------------------------------- rope etc.
+namespace {
+
+int rope_checks(const void* positions, int pos_dtype, int64_t num_tokens, int64_t num_heads,
+                int64_t num_kv_heads, int64_t head_size, const void* cos_sin_cache,
+                int64_t cache_rows, int64_t rot_dim, int dtype) {
+    TLB_REQUIRE(is_float(dtype), "dtype must be float16, bfloat16 or float32");
+    TLB_REQUIRE(is_index(pos_dtype), "positions must be int32 or int64");
+    TLB_REQUIRE(num_tokens > 0, "positions must contain at least one token");
+    TLB_REQUIRE(head_size > 0, "head_size must be positive");
+    TLB_REQUIRE(num_heads >= 0 && num_kv_heads >= 0, "head counts must not be negative");
+    TLB_REQUIRE(rot_dim > 0 && rot_dim % 2 == 0, "rotary dimension must be even and positive");
+    TLB_REQUIRE(rot_dim <= head_size, "rotary dimension must not exceed head_size");
+    TLB_REQUIRE(cache_rows > 0, "cos_sin_cache must have at least one row");
+    TLB_REQUIRE(positions && cos_sin_cache, "tensor pointers must not be null");
+    return TLB_OK;
+}
+
+// 16-byte vectors when every pointer and every row/head offset allows them.
+int pick_vec(int dtype, int64_t head_size, int64_t rot_dim, std::initializer_list<int64_t> strides,
+             std::initializer_list<const void*> ptrs) {
+    const int v = 16 / elem_bytes(dtype);
+    if (head_size % v || (rot_dim / 2) % v) return 1;
+    for (int64_t s : strides)
+        if (s % v) return 1;
+    for (const void* p : ptrs)
+        if (p && !aligned(p, 16)) return 1;
+    return v;
+}
+
+}  // namespace
+
+int tlb_rotary_embedding_neox(void* out, const void* positions, int pos_dtype, const void* query,
+                              void* key, int64_t num_tokens, int64_t num_heads,
+                              int64_t num_kv_heads, int64_t head_size, const void* cos_sin_cache,
+                              int64_t cache_rows, int64_t rot_dim, int64_t query_stride,
+                              int64_t key_stride, int64_t out_stride, int dtype, void* stream) {
+    if (int rc = rope_checks(positions, pos_dtype, num_tokens, num_heads, num_kv_heads, head_size,
+                             cos_sin_cache, cache_rows, rot_dim, dtype))
+        return rc;
+    TLB_REQUIRE(num_heads == 0 || (out && query), "query/out pointers must not be null");
+    TLB_REQUIRE(num_kv_heads == 0 || key, "key pointer must not be null");
+    tlb::RopeCacheParams p{};
+    p.out = out;
+    p.positions = positions;
+    p.query = query;
+    p.key = key;
+    p.cos_sin = cos_sin_cache;
+    p.cache_rows = cache_rows;
+    p.num_tokens = num_tokens;
+    p.query_stride = query_stride;
+    p.key_stride = key_stride;
+    p.out_stride = out_stride;
+    p.num_heads = (int)num_heads;
+    p.num_kv_heads = (int)num_kv_heads;
+    p.head_size = (int)head_size;
+    p.rot_dim = (int)rot_dim;
+    p.block_size = 1;
+    const int vec = pick_vec(dtype, head_size, rot_dim, {query_stride, key_stride, out_stride},
+                             {out, query, key, cos_sin_cache});
+    cudaError_t e = tlb::launch_rope(dtype, pos_dtype, vec, p, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "launching rotary_embedding_neox");
+    return TLB_OK;
+}
+
+namespace {
+int cache_checks(const void* key_cache, const void* value_cache, int64_t num_tokens,
+                 int64_t num_kv_heads, int64_t head_size, int64_t num_blocks, int64_t block_size,
+                 int dtype) {
+    TLB_REQUIRE(is_float(dtype), "dtype must be float16, bfloat16 or float32");
+    TLB_REQUIRE(num_tokens >= 0, "num_tokens must not be negative");
+    TLB_REQUIRE(num_kv_heads > 0 && head_size > 0 && num_blocks > 0 && block_size > 0,
+                "cache sizes must be positive");
+    TLB_REQUIRE(key_cache && value_cache, "cache pointers must not be null");
+    return TLB_OK;
+}
+}  // namespace
+
+int tlb_reshape_and_cache(const void* key, const void* value, void* key_cache, void* value_cache,
+                          const void* slots, int slot_dtype, int64_t num_tokens,
+                          int64_t num_kv_heads, int64_t head_size, int64_t num_blocks,
+                          int64_t block_size, int64_t key_stride, int64_t value_stride, int dtype,
+                          void* stream) {
+    if (int rc = cache_checks(key_cache, value_cache, num_tokens, num_kv_heads, head_size,
+                              num_blocks, block_size, dtype))
+        return rc;
+    TLB_REQUIRE(is_index(slot_dtype), "slot_mapping must be int32 or int64");
+    if (num_tokens == 0) return TLB_OK;
+    TLB_REQUIRE(key && value && slots, "tensor pointers must not be null");
+    tlb::RopeCacheParams p{};
+    p.key = const_cast<void*>(key);
+    p.value = value;
+    p.key_cache = key_cache;
+    p.value_cache = value_cache;
+    p.slots = slots;
+    p.num_tokens = num_tokens;
+    p.key_stride = key_stride;
+    p.value_stride = value_stride;
+    p.num_blocks = num_blocks;
+    p.num_kv_heads = (int)num_kv_heads;
+    p.head_size = (int)head_size;
+    p.rot_dim = 0;
+    p.block_size = (int)block_size;
+    const int vec = pick_vec(dtype, head_size, 0, {key_stride, value_stride},
+                             {key, value, key_cache, value_cache});
+    cudaError_t e = tlb::launch_cache_write(dtype, slot_dtype, false, vec, p,
+                                            reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "launching reshape_and_cache");
+    return TLB_OK;
+}
+
+int tlb_write_kv_cache(const void* key, const void* value, void* key_cache, void* value_cache,
+                       const void* positions, int pos_dtype, const int32_t* block_tables,
+                       int64_t max_blocks_per_seq, int64_t num_tokens, int64_t num_kv_heads,
+                       int64_t head_size, int64_t num_blocks, int64_t block_size,
+                       int64_t key_stride, int64_t value_stride, int dtype, void* stream) {
+    if (int rc = cache_checks(key_cache, value_cache, num_tokens, num_kv_heads, head_size,
+                              num_blocks, block_size, dtype))
+        return rc;
+    TLB_REQUIRE(is_index(pos_dtype), "positions must be int32 or int64");
+    TLB_REQUIRE(max_blocks_per_seq > 0, "block_tables must have at least one column");
+    if (num_tokens == 0) return TLB_OK;
+    TLB_REQUIRE(key && value && positions && block_tables, "tensor pointers must not be null");
+    tlb::RopeCacheParams p{};
+    p.key = const_cast<void*>(key);
+    p.value = value;
+    p.key_cache = key_cache;
+    p.value_cache = value_cache;
+    p.positions = positions;
+    p.block_tables = block_tables;
+    p.max_blocks = (int)max_blocks_per_seq;
+    p.num_tokens = num_tokens;
+    p.key_stride = key_stride;
+    p.value_stride = value_stride;
+    p.num_blocks = num_blocks;
+    p.num_kv_heads = (int)num_kv_heads;
+    p.head_size = (int)head_size;
+    p.rot_dim = 0;
+    p.block_size = (int)block_size;
+    const int vec = pick_vec(dtype, head_size, 0, {key_stride, value_stride},
+                             {key, value, key_cache, value_cache});
+    cudaError_t e = tlb::launch_cache_write(dtype, pos_dtype, true, vec, p,
+                                            reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "launching write_kv_cache");
+    return TLB_OK;
+}
+
+int tlb_rotary_embedding_neox_with_cache(
+    void* out, const void* positions, int pos_dtype, const void* query, void* key,
+    const void* value, void* key_cache, void* value_cache, const void* slots, int slot_dtype,
+    const int32_t* block_tables, int64_t max_blocks_per_seq, int64_t num_tokens, int64_t num_heads, int64_t num_kv_heads, int64_t head_size,
+    const void* cos_sin_cache, int64_t cache_rows, int64_t rot_dim, int64_t num_blocks,
+    int64_t block_size, int64_t query_stride, int64_t key_stride, int64_t value_stride,
+    int64_t out_stride, int dtype, void* stream) {
+    if (int rc = rope_checks(positions, pos_dtype, num_tokens, num_heads, num_kv_heads, head_size,
+                             cos_sin_cache, cache_rows, rot_dim, dtype))
+        return rc;
+    if (int rc = cache_checks(key_cache, value_cache, num_tokens, num_kv_heads, head_size,
+                              num_blocks, block_size, dtype))
+        return rc;
+    const bool by_table = slots == nullptr;
+    if (by_table) {
+        TLB_REQUIRE(block_tables != nullptr && max_blocks_per_seq > 0,
+                    "either slots or block_tables must be given");
+    } else {
+        TLB_REQUIRE(is_index(slot_dtype), "slot_mapping must be int32 or int64");
+    }
+    TLB_REQUIRE(out && query && key && value, "tensor pointers must not be null");
+    tlb::RopeCacheParams p{};
+    p.block_tables = block_tables;
+    p.max_blocks = (int)max_blocks_per_seq;
+    p.out = out;
+    p.positions = positions;
+    p.query = query;
+    p.key = key;
+    p.value = value;
+    p.key_cache = key_cache;
+    p.value_cache = value_cache;
+    p.slots = slots;
+    p.cos_sin = cos_sin_cache;
+    p.cache_rows = cache_rows;
+    p.num_tokens = num_tokens;
+    p.query_stride = query_stride;
+    p.key_stride = key_stride;
+    p.value_stride = value_stride;
+    p.out_stride = out_stride;
+    p.num_blocks = num_blocks;
+    p.num_heads = (int)num_heads;
+    p.num_kv_heads = (int)num_kv_heads;
+    p.head_size = (int)head_size;
+    p.rot_dim = (int)rot_dim;
+    p.block_size = (int)block_size;
+    const int vec =
+        pick_vec(dtype, head_size, rot_dim, {query_stride, key_stride, value_stride, out_stride},
+                 {out, query, key, value, key_cache, value_cache, cos_sin_cache});
+    cudaError_t e = tlb::launch_rope_cache(dtype, pos_dtype, by_table ? TLB_INT64 : slot_dtype,
+                                           by_table, vec, p,
+                                           reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "launching rotary_embedding_neox_with_cache");
+    return TLB_OK;
+}
+
+int tlb_decode_metadata(const int32_t* context_lens, const int32_t* block_tables,
+                        int64_t num_seqs, int64_t max_blocks_per_seq, int64_t block_size,
+                        int64_t* positions_out, int64_t* slots_out, void* stream) {
+    TLB_REQUIRE(num_seqs >= 0 && max_blocks_per_seq > 0 && block_size > 0,
+                "sizes must be positive");
+    if (num_seqs == 0) return TLB_OK;
+    TLB_REQUIRE(context_lens && block_tables && positions_out && slots_out,
+                "tensor pointers must not be null");
+    cudaError_t e = tlb::launch_decode_metadata(context_lens, block_tables, num_seqs,
+                                                (int)max_blocks_per_seq, (int)block_size,
+                                                positions_out, slots_out,
+                                                reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "launching decode_metadata");
+    return TLB_OK;
+}
+
+// ------------------------------------------------------------ block copies
+int tlb_copy_blocks(void* const* caches, int64_t num_caches, const int64_t* pairs,
+                    int64_t num_pairs, int64_t block_bytes, void* stream) {
+    TLB_REQUIRE(num_caches >= 0 && num_pairs >= 0, "counts must not be negative");
+    if (num_caches == 0 || num_pairs == 0) return TLB_OK;
+    TLB_REQUIRE(caches && pairs, "caches and pairs must not be null");
+    TLB_REQUIRE(block_bytes > 0, "block_bytes must be positive");
+    bool vec16 = block_bytes % 16 == 0;
+    for (int64_t c = 0; c < num_caches; ++c) {
+        TLB_REQUIRE(caches[c] != nullptr, "cache pointer %lld is null", (long long)c);
+        if (!aligned(caches[c], 16)) vec16 = false;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    tlb::CopyParams p;
+    p.block_bytes = block_bytes;
+    for (int64_t c0 = 0; c0 < num_caches; c0 += tlb::kCopyMaxCaches) {
+        p.num_caches = (int)std::min<int64_t>(tlb::kCopyMaxCaches, num_caches - c0);
+        for (int c = 0; c < p.num_caches; ++c) {
+            p.dst[c] = static_cast<char*>(caches[c0 + c]);
+            p.src[c] = static_cast<const char*>(caches[c0 + c]);
+        }
+        for (int64_t k0 = 0; k0 < num_pairs; k0 += tlb::kCopyMaxPairs) {
+            p.num_pairs = (int)std::min<int64_t>(tlb::kCopyMaxPairs, num_pairs - k0);
+            std::memcpy(p.pairs, pairs + 2 * k0, sizeof(int64_t) * 2 * p.num_pairs);
+            cudaError_t e = tlb::launch_copy_blocks(p, vec16, st);
+            if (e != cudaSuccess) return cuda_fail(e, "launching copy_blocks");
+        }
+    }
+    return TLB_OK;
+}
+
+int tlb_swap_blocks(const void* src, int src_on_device, void* dst, int dst_on_device,
+                    const int64_t* pairs, int64_t num_pairs, int64_t block_bytes, void* stream) {
+    TLB_REQUIRE(num_pairs >= 0, "num_pairs must not be negative");
+    if (num_pairs == 0) return TLB_OK;
+    TLB_REQUIRE(src && dst && pairs, "pointers must not be null");
+    TLB_REQUIRE(block_bytes > 0, "block_bytes must be positive");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const char* s = static_cast<const char*>(src);
+    char* d = static_cast<char*>(dst);
+    if (!src_on_device && !dst_on_device) {
+        for (int64_t k = 0; k < num_pairs; ++k)
+            std::memcpy(d + pairs[2 * k + 1] * block_bytes, s + pairs[2 * k] * block_bytes,
+                        (size_t)block_bytes);
+        return TLB_OK;
+    }
+    if (src_on_device && dst_on_device) {
+        tlb::CopyParams p;
+        p.block_bytes = block_bytes;
+        p.num_caches = 1;
+        p.dst[0] = d;
+        p.src[0] = s;
+        const bool vec16 = block_bytes % 16 == 0 && aligned(src, 16) && aligned(dst, 16);
+        for (int64_t k0 = 0; k0 < num_pairs; k0 += tlb::kCopyMaxPairs) {
+            p.num_pairs = (int)std::min<int64_t>(tlb::kCopyMaxPairs, num_pairs - k0);
+            std::memcpy(p.pairs, pairs + 2 * k0, sizeof(int64_t) * 2 * p.num_pairs);
+            cudaError_t e = tlb::launch_copy_blocks(p, vec16, st);
+            if (e != cudaSuccess) return cuda_fail(e, "launching swap_blocks");
+        }
+        return TLB_OK;
+    }
+    // Host <-> device: one copy per run of consecutive blocks.
+    const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
+    int64_t k = 0;
+    while (k < num_pairs) {
+        int64_t run = 1;
+        while (k + run < num_pairs && pairs[2 * (k + run)] == pairs[2 * k] + run &&
+               pairs[2 * (k + run) + 1] == pairs[2 * k + 1] + run)
+            ++run;
+        cudaError_t e = cudaMemcpyAsync(d + pairs[2 * k + 1] * block_bytes,
+                                        s + pairs[2 * k] * block_bytes,
+                                        (size_t)(run * block_bytes), kind, st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync in swap_blocks");
+        k += run;
+    }
+    return TLB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+// Internal launch interface between the C ABI (abi.cu) and the kernel files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tlb {
+
+// ------------------------------------------------------------ attention
+namespace attn {
+
+constexpr int kConsumerWarps = 4;   // warps that run the mma / softmax
+constexpr int kTileRows = 16;       // tokens per warp tile (mma k / n extent)
+constexpr int kStageRows = kConsumerWarps * kTileRows;  // tokens per pipeline stage
+constexpr int kGMax = 16;           // largest query-head group on the tensor-core path
+constexpr int kMaxCtasPerSm = 2;    // bound used to size the partial-result workspace
+constexpr int kWorkspaceHeader = 256;
+
+struct TcParams {
+    void* out;
+    const void* query;
+    const int32_t* block_tables;
+    const int32_t* seq_lens;
+    float* ws_o;              // [2 * grid][gpad][head_dim] unnormalised partial outputs
+    float* ws_ml;             // [2 * grid][gpad][2] (running max, running sum) per partial
+    unsigned int* counters;   // [num_seqs * num_kv_heads] arrival counters (self-resetting)
+    long long num_blocks;
+    int num_seqs;
+    int num_heads;
+    int num_kv_heads;
+    int group;                // num_heads / num_kv_heads
+    int block_size;
+    int max_blocks;
+    int min_units;            // fewest KV blocks a CTA is given before more CTAs join
+    float scale_log2;         // softmax scale * log2(e)
+};
+
+struct GenericParams {
+    void* out;
+    const void* query;
+    const void* key_cache;
+    const void* value_cache;
+    const int32_t* block_tables;
+    const int32_t* seq_lens;
+    long long num_blocks;
+    int num_seqs;
+    int num_heads;
+    int num_kv_heads;
+    int group;
+    int head_dim;
+    int block_size;
+    int max_blocks;
+    float scale_log2;
+};
+
+// Returns true when the tensor-core path serves this shape / dtype.
+bool tc_supported(int dtype, int head_dim, int group, int block_size);
+// Heads per partial slot in the workspace for a group size.
+int tc_gpad(int group);
+// Number of CTAs the tensor-core kernel launches on `device` (persistent grid).
+int tc_grid(int device, int dtype, int head_dim, int group, cudaError_t* err);
+
+cudaError_t launch_tc(int dtype, int head_dim, int group, const TcParams& p,
+                      const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid,
+                      cudaStream_t stream);
+cudaError_t launch_generic(int dtype, const GenericParams& p, cudaStream_t stream);
+
+}  // namespace attn
+
+// ---------------------------------------------------- rope + cache writes
+struct RopeCacheParams {
+    void* out;                 // rotated query (may be null when no query work)
+    const void* positions;
+    const void* query;
+    void* key;
+    const void* value;
+    void* key_cache;
+    void* value_cache;
+    const void* slots;         // slot mapping, or null with block_tables
+    const int32_t* block_tables;
+    const void* cos_sin;
+    long long cache_rows;
+    long long num_tokens;
+    long long query_stride, key_stride, value_stride, out_stride;
+    long long num_blocks;
+    int max_blocks;
+    int num_heads;
+    int num_kv_heads;
+    int head_size;
+    int rot_dim;
+    int block_size;
+};
+
+// Rope only (query -> out, key in place).
+cudaError_t launch_rope(int dtype, int pos_dtype, int vec, const RopeCacheParams& p,
+                        cudaStream_t stream);
+// Rope + write rotated key and value into the cache through `slots`, or
+// through block_tables[t, pos / block_size] when by_block_table is set.
+cudaError_t launch_rope_cache(int dtype, int pos_dtype, int slot_dtype, bool by_block_table,
+                              int vec, const RopeCacheParams& p, cudaStream_t stream);
+// Cache write only: `slots` (slot_dtype) or positions + block_tables.
+cudaError_t launch_cache_write(int dtype, int index_dtype, bool by_block_table, int vec,
+                               const RopeCacheParams& p, cudaStream_t stream);
+cudaError_t launch_decode_metadata(const int32_t* context_lens, const int32_t* block_tables,
+                                   long long num_seqs, int max_blocks, int block_size,
+                                   int64_t* positions, int64_t* slots, cudaStream_t stream);
+
+// ------------------------------------------------------------ block copies
+constexpr int kCopyMaxCaches = 128;
+constexpr int kCopyMaxPairs = 1024;
+struct CopyParams {
+    long long block_bytes;
+    int num_caches;
+    int num_pairs;
+    char* dst[kCopyMaxCaches];
+    const char* src[kCopyMaxCaches];
+    long long pairs[2 * kCopyMaxPairs];
+};
+cudaError_t launch_copy_blocks(const CopyParams& p, bool vec16, cudaStream_t stream);
+
+}  // namespace tlb

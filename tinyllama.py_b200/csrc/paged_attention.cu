@@ -1,0 +1,947 @@
+// Paged-attention decode for sm_100a.
+//
+// Reference semantics (cscr/attention_kernel.cu:24-107, launch :111-150):
+// for every sequence s and query head h, softmax(scale * q[s,h] . K_s^T) V_s
+// over the first seq_lens[s] tokens of the sequence, where token t lives in
+// physical block block_tables[s, t / block_size] at offset t % block_size and
+// uses KV head h / (num_heads / num_kv_heads). Tokens whose block id is
+// negative are skipped; an empty softmax gives zeros (:102).
+//
+// Tensor-core path (fp16 / bf16, head_dim 64 or 128, group <= 16):
+//   * Work is the flat list of (sequence, kv head, KV block) units, cut into
+//     equal contiguous ranges, one per persistent CTA ("stream-K"), so every
+//     CTA streams the same number of KV bytes whatever the length mix.
+//   * Inside a CTA one producer warp walks its range and, per pipeline stage
+//     of 64 tokens, issues 2-D TMA loads (128-byte swizzle, evict-first L2
+//     policy) of each KV block straight from the paged cache, plus a bulk
+//     load of the query group when a new (sequence, kv head) piece starts.
+//   * Four consumer warps each take 16 tokens of a stage: S = Q K^T with
+//     mma.m16n8k16 (query heads of one KV head folded into the 16 rows, so a
+//     KV byte is read once for the whole group), an fp32 online softmax in
+//     registers with quad shuffles, and O^T += V^T P^T with the softmax
+//     probabilities fed straight from the S accumulators.
+//   * A piece that covers a whole (sequence, kv head) is normalised and
+//     written directly. A piece cut by a range boundary writes an fp32
+//     partial (O, max, sum); the CTA that arrives last on that sequence's
+//     counter merges the partials and writes the output, then the counter
+//     is back at zero (atomicInc wrap), so no second kernel is launched.
+//
+// Generic path (fp32, other head sizes / groups / block sizes): one CTA per
+// (sequence, kv head, head chunk), warps stride over tokens with the query
+// group folded, fp32 CUDA-core arithmetic.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <mutex>
+
+namespace tlb {
+namespace attn {
+
+namespace {
+
+enum : int {
+    kPieceStart = 1,
+    kPieceEnd = 2,
+    kPieceComplete = 4,
+    kTerminate = 8,
+};
+
+struct StageDesc {
+    int seq;
+    int kvh;
+    int tok0;        // token index (within the sequence) of stage row 0
+    int nrows;       // rows loaded in this stage (blocks * block_size)
+    int seqlen;      // clamped context length of the sequence
+    unsigned invalid_mask;  // bit i: block i of this stage was not loaded
+    int flags;
+    int slot;        // partial slot of this piece (when not complete)
+    int nsplits;     // pieces the (sequence, kv head) is cut into
+    int jfirst;      // first CTA holding a piece of it
+    int first_slot1; // that CTA stored its piece in its second slot
+    int u;           // sequence * num_kv_heads + kv head
+};
+
+template <int D, int NT, int NSTAGE>
+struct TcLayout {
+    static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
+    static constexpr int kChunkBytes = kStageRows * 128;
+    static constexpr int kStageKV = kStageRows * D * 2;  // bytes of K (or V) per stage
+    static constexpr int kQBytes = kGMax * D * 2;
+    static constexpr int kGP = 8 * NT;                 // padded heads per piece
+    static constexpr int kOFloats = kConsumerWarps * kGP * D;
+    static constexpr int kOffK = 0;
+    static constexpr int kOffV = kOffK + NSTAGE * kStageKV;
+    static constexpr int kOffQ = kOffV + NSTAGE * kStageKV;
+    static constexpr int kOffO = kOffQ + NSTAGE * kQBytes;
+    static constexpr int kOffM = kOffO + kOFloats * 4;
+    static constexpr int kOffL = kOffM + kConsumerWarps * kGP * 4;
+    static constexpr int kOffDesc = kOffL + kConsumerWarps * kGP * 4;
+    static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
+    static constexpr int kOffMisc = kOffBar + 2 * NSTAGE * 8;
+    static constexpr int kMiscInts = 64;
+    static constexpr int kBytes = kOffMisc + kMiscInts * 4;
+    static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+};
+
+// Block-wide inclusive scan of a 64-bit value over blockDim.x threads.
+__device__ __forceinline__ long long block_incl_scan(long long v, long long* warp_sums,
+                                                     long long* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        long long n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_sums[warp] = v;
+    __syncthreads();
+    long long before = 0, all = 0;
+    for (int w = 0; w < nwarps; ++w) {
+        const long long ws = warp_sums[w];
+        if (w < warp) before += ws;
+        all += ws;
+    }
+    __syncthreads();
+    *total = all;
+    return v + before;
+}
+
+// CTA whose unit range [floor(j W / P), floor((j+1) W / P)) contains unit x.
+__device__ __forceinline__ int cta_of(long long x, long long W, int P) {
+    return (int)(((x + 1) * (long long)P - 1) / W);
+}
+__device__ __forceinline__ long long range_start(int j, long long W, int P) {
+    return (long long)j * W / P;
+}
+
+// One stage job of the producer: a run of <= blocks_per_stage KV blocks of a
+// single (sequence, kv head) piece.
+struct Job {
+    int s, h, cb, nblk;
+    int nb;          // blocks of the sequence (clamped)
+    int seqlen;
+    int b_lo, b_hi;  // block range of the piece
+    long long pre;   // KV blocks of all sequences before s
+    bool valid;
+};
+
+}  // namespace
+
+template <typename T, int D, int NT, int NSTAGE>
+__global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
+    paged_attention_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
+                              const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
+    using L = TcLayout<D, NT, NSTAGE>;
+    constexpr int GP = L::kGP;
+    constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
+    constexpr int kConsumerThreads = kConsumerWarps * 32;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    const uint32_t sbase = smem_u32(smem);
+
+    float* sO = reinterpret_cast<float*>(smem + L::kOffO);
+    float* sM = reinterpret_cast<float*>(smem + L::kOffM);
+    float* sL = reinterpret_cast<float*>(smem + L::kOffL);
+    StageDesc* sDesc = reinterpret_cast<StageDesc*>(smem + L::kOffDesc);
+    const uint32_t bar_full = sbase + L::kOffBar;           // NSTAGE x 8 bytes
+    const uint32_t bar_empty = bar_full + NSTAGE * 8;       // NSTAGE x 8 bytes
+    long long* sScan = reinterpret_cast<long long*>(smem + L::kOffMisc);  // 8 warp sums
+    int* sMisc = reinterpret_cast<int*>(smem + L::kOffMisc + 8 * 8);
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int S = p.num_seqs;
+    const int KVH = p.num_kv_heads;
+    const int G = p.group;
+    const int bs = p.block_size;
+    const int cap_tokens = p.max_blocks * bs;
+
+    if (tid == 0) {
+        for (int i = 0; i < NSTAGE; ++i) {
+            mbar_init(bar_full + 8 * i, 1);
+            mbar_init(bar_empty + 8 * i, kConsumerWarps);
+        }
+        fence_mbar_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == kConsumerWarps && lane == 0) {
+        prefetch_tensormap(&tm_k);
+        prefetch_tensormap(&tm_v);
+    }
+
+    // ---- pass 1: total KV blocks; zero the outputs of empty sequences.
+    long long my_blocks = 0;
+    unsigned bad_len = 0;
+    for (int s = tid; s < S; s += blockDim.x) {
+        int len = p.seq_lens[s];
+        if (len > cap_tokens) { bad_len = 1; len = cap_tokens; }
+        if (len > 0) my_blocks += (len + bs - 1) / bs;
+    }
+    if (bad_len) flag_status(TLB_STATUS_SEQ_TOO_LONG);
+    long long total_blocks;
+    block_incl_scan(my_blocks, sScan, &total_blocks);
+
+    T* out = reinterpret_cast<T*>(p.out);
+    for (int s = blockIdx.x; s < S; s += gridDim.x) {
+        if (p.seq_lens[s] <= 0) {
+            const long long base = (long long)s * p.num_heads * D;
+            for (int e = tid; e < p.num_heads * D; e += blockDim.x)
+                out[base + e] = Elem<T>::from_f(0.f);
+        }
+    }
+
+    const long long W = total_blocks * KVH;
+    if (W == 0) return;
+    int P = (int)gridDim.x;
+    {
+        const long long want = (W + p.min_units - 1) / p.min_units;
+        if (want < P) P = (int)(want > 0 ? want : 1);
+    }
+    const int j = blockIdx.x;
+    if (j >= P) return;
+    const long long ustart = range_start(j, W, P);
+    const long long uend = range_start(j + 1, W, P);
+    if (ustart >= uend) return;
+
+    // ---- pass 2: locate the sequence holding unit `ustart`.
+    if (tid == 0) sMisc[0] = -1;
+    __syncthreads();
+    {
+        long long base = 0;
+        for (int c0 = 0; c0 < S; c0 += blockDim.x) {
+            const int s = c0 + tid;
+            long long nb = 0;
+            if (s < S) {
+                int len = min(p.seq_lens[s], cap_tokens);
+                nb = len > 0 ? (len + bs - 1) / bs : 0;
+            }
+            long long chunk_total;
+            const long long incl = block_incl_scan(nb, sScan, &chunk_total);
+            const long long excl = incl - nb;
+            if (nb > 0 && (base + excl) * KVH <= ustart && ustart < (base + incl) * KVH) {
+                sMisc[0] = s;
+                reinterpret_cast<long long*>(sMisc)[1] = base + excl;
+            }
+            __syncthreads();
+            base += chunk_total;
+            if (base * KVH > ustart) break;
+        }
+    }
+    __syncthreads();
+    const int s_first = sMisc[0];
+    const long long pre_first = reinterpret_cast<long long*>(sMisc)[1];
+    if (s_first < 0) return;  // cannot happen for ustart < W; never walk from garbage
+
+    if (warp == kConsumerWarps) {
+        // ===================================================== producer warp
+        const int bps = kStageRows / bs;  // blocks per stage
+        const uint64_t pol = l2_policy_evict_first();
+        const int P_ = P;
+        const T* query = reinterpret_cast<const T*>(p.query);
+
+        auto seq_blocks = [&](int s, int& seqlen) -> int {
+            int len = min(p.seq_lens[s], cap_tokens);
+            seqlen = len > 0 ? len : 0;
+            return len > 0 ? (len + bs - 1) / bs : 0;
+        };
+        // First job of the piece that starts at unit x (x inside sequence s).
+        auto piece_job = [&](long long x, int s, long long pre) -> Job {
+            Job jb;
+            jb.valid = false;
+            if (x >= uend || s >= S) return jb;
+            int seqlen;
+            int nb = seq_blocks(s, seqlen);
+            while (nb == 0) {  // skip empty sequences
+                if (++s >= S) return jb;
+                nb = seq_blocks(s, seqlen);
+            }
+            const long long rel = x - pre * KVH;
+            jb.s = s;
+            jb.h = (int)(rel / nb);
+            jb.b_lo = (int)(rel % nb);
+            const long long u_first = pre * KVH + (long long)jb.h * nb;
+            jb.b_hi = (int)min((long long)nb, uend - u_first);
+            jb.cb = jb.b_lo;
+            jb.nblk = min(bps, jb.b_hi - jb.cb);
+            jb.nb = nb;
+            jb.seqlen = seqlen;
+            jb.pre = pre;
+            jb.valid = true;
+            return jb;
+        };
+        auto next_job = [&](const Job& jb) -> Job {
+            if (jb.cb + jb.nblk < jb.b_hi) {
+                Job n = jb;
+                n.cb = jb.cb + jb.nblk;
+                n.nblk = min(bps, jb.b_hi - n.cb);
+                return n;
+            }
+            // piece finished: next unit
+            const long long x = jb.pre * KVH + (long long)jb.h * jb.nb + jb.b_hi;
+            if (jb.h + 1 < KVH) return piece_job(x, jb.s, jb.pre);
+            return piece_job(x, jb.s + 1, jb.pre + jb.nb);
+        };
+
+        Job job = piece_job(ustart, s_first, pre_first);
+        int bid = -1;
+        if (job.valid && lane < job.nblk)
+            bid = p.block_tables[(long long)job.s * p.max_blocks + job.cb + lane];
+        int stage = 0;
+        uint32_t phase = 0;
+        bool first_piece = true;
+        bool ok = true;
+        while (job.valid) {
+            const Job nxt = next_job(job);
+            int nbid = -1;
+            if (nxt.valid && lane < nxt.nblk)
+                nbid = p.block_tables[(long long)nxt.s * p.max_blocks + nxt.cb + lane];
+
+            bool waited = true;
+            if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
+            waited = __shfl_sync(0xffffffffu, waited, 0);
+            if (!waited) {
+                if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
+                ok = false;
+                break;
+            }
+            const bool in_range = lane < job.nblk;
+            const bool valid = in_range && bid >= 0 && (long long)bid < p.num_blocks;
+            if (in_range && (long long)bid >= p.num_blocks) flag_status(TLB_STATUS_BAD_BLOCK_ID);
+            const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+            const bool piece_start = job.cb == job.b_lo;
+            const bool piece_end = job.cb + job.nblk == job.b_hi;
+            if (lane == 0) {
+                StageDesc& d = sDesc[stage];
+                d.seq = job.s;
+                d.kvh = job.h;
+                d.tok0 = job.cb * bs;
+                d.nrows = job.nblk * bs;
+                d.seqlen = job.seqlen;
+                d.invalid_mask = (~vmask) & ((1u << job.nblk) - 1u);
+                const bool complete = job.b_lo == 0 && job.b_hi == job.nb;
+                d.flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
+                          (complete ? kPieceComplete : 0);
+                d.u = job.s * KVH + job.h;
+                if (!complete) {
+                    const long long u_first = job.pre * KVH + (long long)job.h * job.nb;
+                    const int jf = cta_of(u_first, W, P_);
+                    const int jl = cta_of(u_first + job.nb - 1, W, P_);
+                    d.nsplits = jl - jf + 1;
+                    d.jfirst = jf;
+                    d.first_slot1 = range_start(jf, W, P_) < u_first ? 1 : 0;
+                    d.slot = 2 * j + (first_piece ? 0 : 1);
+                } else {
+                    d.nsplits = 1;
+                    d.jfirst = j;
+                    d.first_slot1 = 0;
+                    d.slot = 2 * j;
+                }
+                const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
+                                       (piece_start ? (uint32_t)(G * D * 2) : 0u);
+                mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
+            }
+            __syncwarp();
+            if (valid) {
+                const uint32_t fb = bar_full + 8 * stage;
+                const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV + lane * bs * 128;
+                const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV + lane * bs * 128;
+                const int32_t y = (int32_t)(((long long)bid * KVH + job.h) * bs);
+#pragma unroll
+                for (int c = 0; c < L::kChunks; ++c) {
+                    tma_load_2d(kdst + c * L::kChunkBytes, &tm_k, c * 64, y, fb, pol);
+                    tma_load_2d(vdst + c * L::kChunkBytes, &tm_v, c * 64, y, fb, pol);
+                }
+            }
+            if (piece_start && lane == 0) {
+                const T* qsrc = query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
+                bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2),
+                          bar_full + 8 * stage);
+            }
+            if (piece_end) first_piece = false;
+            if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
+            job = nxt;
+            bid = nbid;
+        }
+        if (ok) {
+            bool waited = true;
+            if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
+            waited = __shfl_sync(0xffffffffu, waited, 0);
+            if (lane == 0) {
+                if (waited) {
+                    sDesc[stage].flags = kTerminate;
+                    mbar_arrive(bar_full + 8 * stage);
+                } else {
+                    flag_status(TLB_STATUS_WAIT_TIMEOUT);
+                }
+            }
+        } else {
+            // A wait gave up: let the copies already issued land before the
+            // CTA's shared memory is released. Stage `stage` was not issued;
+            // the NSTAGE-1 before it may have been.
+            if (lane == 0) {
+                int st = stage;
+                uint32_t ph = phase;
+                for (int k = 0; k < NSTAGE - 1; ++k) {
+                    if (st == 0) { st = NSTAGE - 1; ph ^= 1; } else { --st; }
+                    mbar_wait_bounded(bar_full + 8 * st, ph);
+                }
+            }
+        }
+        return;
+    }
+
+    // ======================================================== consumer warps
+    const int g = lane >> 2;  // row group of the mma fragments
+    const int q4 = lane & 3;  // thread in group
+    const uint32_t mi = lane >> 3;
+    const int ld_row = (lane & 7) + ((mi >> 1) << 3);  // ldmatrix row within a 16-row tile
+    const int ld_kk = (int)(mi & 1);
+    const int r0 = warp * kTileRows;
+
+    float m_run[2], l_run[2];
+    float o[NT][KS][4];
+    uint32_t qa[KS][4];
+    m_run[0] = m_run[1] = -INFINITY;
+    l_run[0] = l_run[1] = 0.f;
+
+    int stage = 0;
+    uint32_t phase = 0;
+    while (true) {
+        bool got = true;
+        got = mbar_wait_bounded(bar_full + 8 * stage, phase);
+        if (!got) {
+            if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
+            break;
+        }
+        const StageDesc d = sDesc[stage];
+        if (d.flags & kTerminate) break;
+
+        if (d.flags & kPieceStart) {
+            const T* sq = reinterpret_cast<const T*>(smem + L::kOffQ + stage * L::kQBytes);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const int c0 = ks * 16 + 2 * q4;
+                qa[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(sq + g * D + c0) : 0u;
+                qa[ks][1] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(sq + (g + 8) * D + c0) : 0u;
+                qa[ks][2] = g < G ? *reinterpret_cast<const uint32_t*>(sq + g * D + c0 + 8) : 0u;
+                qa[ks][3] =
+                    g + 8 < G ? *reinterpret_cast<const uint32_t*>(sq + (g + 8) * D + c0 + 8) : 0u;
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) o[nt][mt][e] = 0.f;
+            m_run[0] = m_run[1] = -INFINITY;
+            l_run[0] = l_run[1] = 0.f;
+        }
+
+        // Valid rows of this warp's 16-token tile.
+        bool rv = false;
+        if (lane < 16) {
+            const int r = r0 + lane;
+            rv = r < d.nrows && d.tok0 + r < d.seqlen && !((d.invalid_mask >> (r / bs)) & 1u);
+        }
+        const unsigned vmask = __ballot_sync(0xffffffffu, rv) & 0xffffu;
+
+        if (vmask != 0u) {
+            const uint32_t kbase = sbase + L::kOffK + stage * L::kStageKV;
+            const uint32_t vbase = sbase + L::kOffV + stage * L::kStageKV;
+            if (vmask != 0xffffu) {
+                // Rows that hold no token of this piece may contain anything
+                // (stale stage data, unwritten cache slots): zero V there so
+                // that P = 0 really contributes nothing.
+                uint8_t* vrow = smem + L::kOffV + stage * L::kStageKV;
+                for (int idx = lane; idx < 16 * L::kChunks * 8; idx += 32) {
+                    const int r = idx / (L::kChunks * 8);
+                    const int c = (idx / 8) % L::kChunks;
+                    const int k = idx & 7;
+                    if (!((vmask >> r) & 1u))
+                        *reinterpret_cast<uint4*>(vrow + c * L::kChunkBytes + (r0 + r) * 128 + k * 16) =
+                            make_uint4(0u, 0u, 0u, 0u);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+
+            // ---- S = Q K^T for 16 tokens (two 8-token n-tiles).
+            float s_acc[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s_acc[n][e] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const int c = ks >> 2;
+                const int kk = ((ks & 3) << 1) + ld_kk;
+                const int row = r0 + ld_row;
+                const uint32_t addr =
+                    kbase + c * L::kChunkBytes + row * 128 + ((kk ^ (row & 7)) << 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(addr, b0, b1, b2, b3);
+                mma16816<T>(s_acc[0], qa[ks], b0, b1);
+                mma16816<T>(s_acc[1], qa[ks], b2, b3);
+            }
+
+            // ---- online softmax (log2 domain); heads g (and g + 8).
+            float x[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int tok = n * 8 + 2 * q4 + (e & 1);
+                    x[n][e] = ((vmask >> tok) & 1u) ? s_acc[n][e] * p.scale_log2 : -INFINITY;
+                }
+            float alpha[2];
+            float pr[2][4];
+#pragma unroll
+            for (int hh = 0; hh < NT; ++hh) {
+                float mx = fmaxf(fmaxf(x[0][2 * hh], x[0][2 * hh + 1]),
+                                 fmaxf(x[1][2 * hh], x[1][2 * hh + 1]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float m_new = fmaxf(m_run[hh], mx);
+                const float mu = m_new == -INFINITY ? 0.f : m_new;
+                alpha[hh] = exp2f(m_run[hh] - mu);
+                float rs = 0.f;
+#pragma unroll
+                for (int n = 0; n < 2; ++n)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float pv = exp2f(x[n][2 * hh + e] - mu);
+                        pr[n][2 * hh + e] = pv;
+                        rs += pv;
+                    }
+                l_run[hh] = l_run[hh] * alpha[hh] + rs;
+                m_run[hh] = m_new;
+            }
+            // Rescale O^T columns (heads nt*8 + 2*q4 + {0,1}) by their alphas.
+            const bool need = __any_sync(0xffffffffu, alpha[0] != 1.f || (NT == 2 && alpha[1] != 1.f));
+            if (need) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const float a0 = __shfl_sync(0xffffffffu, alpha[nt], (2 * q4) * 4);
+                    const float a1 = __shfl_sync(0xffffffffu, alpha[nt], (2 * q4 + 1) * 4);
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        o[nt][mt][0] *= a0;
+                        o[nt][mt][1] *= a1;
+                        o[nt][mt][2] *= a0;
+                        o[nt][mt][3] *= a1;
+                    }
+                }
+            }
+            // P^T as the B operand: tokens (2q, 2q+1) and (8+2q, 8+2q+1) of head g.
+            uint32_t pb[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                pb[nt][0] = pack2<T>(pr[0][2 * nt], pr[0][2 * nt + 1]);
+                pb[nt][1] = pack2<T>(pr[1][2 * nt], pr[1][2 * nt + 1]);
+            }
+            // ---- O^T += V^T P^T, one 16-wide slice of head_dim per m-tile.
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                const int c = mt >> 2;
+                const int kk = ((mt & 3) << 1) + ld_kk;
+                const int row = r0 + ld_row;
+                const uint32_t addr =
+                    vbase + c * L::kChunkBytes + row * 128 + ((kk ^ (row & 7)) << 4);
+                uint32_t a[4];
+                ldsm_x4_trans(addr, a[0], a[1], a[2], a[3]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma16816<T>(o[nt][mt], a, pb[nt][0], pb[nt][1]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
+        if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
+
+        if (!(d.flags & kPieceEnd)) continue;
+
+        // ================= piece end: merge the four warps' (m, l, O) =====
+        float lsum[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            float v = l_run[hh];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            lsum[hh] = v;
+        }
+        if (q4 == 0) {
+            sM[warp * GP + g] = m_run[0];
+            sL[warp * GP + g] = lsum[0];
+            if (NT == 2) {
+                sM[warp * GP + 8 + g] = m_run[1];
+                sL[warp * GP + 8 + g] = lsum[1];
+            }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                const int h0 = nt * 8 + 2 * q4;
+                const int d0 = mt * 16 + g;
+                float* base = sO + (warp * GP + h0) * D + d0;
+                base[0] = o[nt][mt][0];
+                base[D] = o[nt][mt][1];
+                base[8] = o[nt][mt][2];
+                base[D + 8] = o[nt][mt][3];
+            }
+        named_bar_sync(1, kConsumerThreads);
+
+        const bool complete = (d.flags & kPieceComplete) != 0;
+        const long long out_base = ((long long)d.seq * p.num_heads + (long long)d.kvh * G) * D;
+        for (int e = tid; e < G * D; e += kConsumerThreads) {
+            const int h = e / D, dd = e - (e / D) * D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sM[w * GP + h]);
+            float acc = 0.f, lt = 0.f;
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) {
+                    const float wt = exp2f(sM[w * GP + h] - M);
+                    acc += wt * sO[(w * GP + h) * D + dd];
+                    lt += wt * sL[w * GP + h];
+                }
+            }
+            if (complete) {
+                out[out_base + e] = Elem<T>::from_f(lt > 0.f ? acc / lt : 0.f);
+            } else {
+                p.ws_o[((long long)d.slot * GP + h) * D + dd] = acc;
+                if (dd == 0) {
+                    p.ws_ml[((long long)d.slot * GP + h) * 2 + 0] = M;
+                    p.ws_ml[((long long)d.slot * GP + h) * 2 + 1] = lt;
+                }
+            }
+        }
+        if (!complete) {
+            __threadfence();
+            named_bar_sync(1, kConsumerThreads);
+            if (tid == 0) {
+                const unsigned old = atomicInc(p.counters + d.u, (unsigned)(d.nsplits - 1));
+                sMisc[8] = old == (unsigned)(d.nsplits - 1) ? 1 : 0;
+            }
+            named_bar_sync(1, kConsumerThreads);
+            if (sMisc[8]) {
+                // Last piece of this (sequence, kv head) to finish: merge all.
+                __threadfence();
+                const int n = d.nsplits;
+                const int cap = L::kOFloats / 2;  // floats for maxima, same for sums
+                float* wM = sO;
+                float* wL = sO + cap;
+                if (n * GP <= cap) {
+                    for (int i = tid; i < n * G; i += kConsumerThreads) {
+                        const int k = i / G, h = i - (i / G) * G;
+                        const int slot = 2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
+                        wM[k * GP + h] = __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2 + 0);
+                        wL[k * GP + h] = __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2 + 1);
+                    }
+                    named_bar_sync(1, kConsumerThreads);
+                    if (tid < G) {
+                        const int h = tid;
+                        float M = -INFINITY;
+                        for (int k = 0; k < n; ++k) M = fmaxf(M, wM[k * GP + h]);
+                        float lt = 0.f;
+                        for (int k = 0; k < n; ++k) {
+                            const float wt = M == -INFINITY ? 0.f : exp2f(wM[k * GP + h] - M);
+                            wM[k * GP + h] = wt;
+                            lt += wt * wL[k * GP + h];
+                        }
+                        sL[h] = lt > 0.f ? 1.f / lt : 0.f;
+                    }
+                    named_bar_sync(1, kConsumerThreads);
+                    for (int e = tid; e < G * D; e += kConsumerThreads) {
+                        const int h = e / D, dd = e - (e / D) * D;
+                        float acc = 0.f;
+                        for (int k = 0; k < n; ++k) {
+                            const int slot =
+                                2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
+                            acc += wM[k * GP + h] *
+                                   __ldcg(p.ws_o + ((long long)slot * GP + h) * D + dd);
+                        }
+                        out[out_base + e] = Elem<T>::from_f(acc * sL[h]);
+                    }
+                } else {
+                    for (int e = tid; e < G * D; e += kConsumerThreads) {
+                        const int h = e / D, dd = e - (e / D) * D;
+                        float M = -INFINITY;
+                        for (int k = 0; k < n; ++k) {
+                            const int slot =
+                                2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
+                            M = fmaxf(M, __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2));
+                        }
+                        float acc = 0.f, lt = 0.f;
+                        if (M != -INFINITY) {
+                            for (int k = 0; k < n; ++k) {
+                                const int slot =
+                                    2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
+                                const float wt =
+                                    exp2f(__ldcg(p.ws_ml + ((long long)slot * GP + h) * 2) - M);
+                                acc += wt * __ldcg(p.ws_o + ((long long)slot * GP + h) * D + dd);
+                                lt += wt * __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2 + 1);
+                            }
+                        }
+                        out[out_base + e] = Elem<T>::from_f(lt > 0.f ? acc / lt : 0.f);
+                    }
+                }
+            }
+        }
+        named_bar_sync(1, kConsumerThreads);
+    }
+}
+
+// ============================================================= generic path
+template <typename T, int NPL, int HG>
+__global__ void __launch_bounds__(256) paged_attention_generic_kernel(const GenericParams p) {
+    constexpr int kWarps = 8;
+    extern __shared__ float gsm[];
+    const int D = p.head_dim;
+    float* q_s = gsm;                         // [HG][32 * NPL]
+    float* o_s = q_s + HG * 32 * NPL;         // [kWarps][HG][32 * NPL]
+    float* m_s = o_s + kWarps * HG * 32 * NPL;  // [kWarps][HG]
+    float* l_s = m_s + kWarps * HG;           // [kWarps][HG]
+
+    const int s = blockIdx.x;
+    const int kvh = blockIdx.y;
+    const int h0 = blockIdx.z * HG;
+    const int G = p.group;
+    const int nh = min(HG, G - h0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const T* query = reinterpret_cast<const T*>(p.query);
+    const T* kc = reinterpret_cast<const T*>(p.key_cache);
+    const T* vc = reinterpret_cast<const T*>(p.value_cache);
+    T* out = reinterpret_cast<T*>(p.out);
+
+    for (int e = tid; e < HG * 32 * NPL; e += blockDim.x) {
+        const int hh = e / (32 * NPL), dd = e % (32 * NPL);
+        float v = 0.f;
+        if (hh < nh && dd < D)
+            v = Elem<T>::to_f(query[((long long)s * p.num_heads + (long long)kvh * G + h0 + hh) * D + dd]);
+        q_s[e] = v;
+    }
+    __syncthreads();
+
+    const int cap = p.max_blocks * p.block_size;
+    int len = p.seq_lens[s];
+    if (len > cap) {
+        if (tid == 0) flag_status(TLB_STATUS_SEQ_TOO_LONG);
+        len = cap;
+    }
+
+    float m[HG], l[HG], acc[HG][NPL];
+#pragma unroll
+    for (int hh = 0; hh < HG; ++hh) {
+        m[hh] = -INFINITY;
+        l[hh] = 0.f;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) acc[hh][i] = 0.f;
+    }
+
+    for (int t = warp; t < len; t += kWarps) {
+        const int bid = p.block_tables[(long long)s * p.max_blocks + t / p.block_size];
+        if (bid < 0) continue;
+        if ((long long)bid >= p.num_blocks) {
+            if (lane == 0) flag_status(TLB_STATUS_BAD_BLOCK_ID);
+            continue;
+        }
+        const long long row =
+            (((long long)bid * p.num_kv_heads + kvh) * p.block_size + t % p.block_size) * D;
+        float kv[NPL];
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const int dd = lane + 32 * i;
+            kv[i] = dd < D ? Elem<T>::to_f(kc[row + dd]) : 0.f;
+        }
+        float pw[HG], al[HG];
+#pragma unroll
+        for (int hh = 0; hh < HG; ++hh) {
+            float part = 0.f;
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) part += q_s[hh * 32 * NPL + lane + 32 * i] * kv[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            const float sc = part * p.scale_log2;
+            const float mn = fmaxf(m[hh], sc);
+            al[hh] = exp2f(m[hh] - mn);
+            pw[hh] = exp2f(sc - mn);
+            l[hh] = l[hh] * al[hh] + pw[hh];
+            m[hh] = mn;
+        }
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const int dd = lane + 32 * i;
+            const float vv = dd < D ? Elem<T>::to_f(vc[row + dd]) : 0.f;
+#pragma unroll
+            for (int hh = 0; hh < HG; ++hh) acc[hh][i] = acc[hh][i] * al[hh] + pw[hh] * vv;
+        }
+    }
+
+    if (lane == 0) {
+#pragma unroll
+        for (int hh = 0; hh < HG; ++hh) {
+            m_s[warp * HG + hh] = m[hh];
+            l_s[warp * HG + hh] = l[hh];
+        }
+    }
+#pragma unroll
+    for (int hh = 0; hh < HG; ++hh)
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) o_s[(warp * HG + hh) * 32 * NPL + lane + 32 * i] = acc[hh][i];
+    __syncthreads();
+
+    for (int e = tid; e < nh * D; e += blockDim.x) {
+        const int hh = e / D, dd = e % D;
+        float M = -INFINITY;
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w * HG + hh]);
+        float a = 0.f, lt = 0.f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < kWarps; ++w) {
+                const float wt = exp2f(m_s[w * HG + hh] - M);
+                a += wt * o_s[(w * HG + hh) * 32 * NPL + dd];
+                lt += wt * l_s[w * HG + hh];
+            }
+        }
+        out[((long long)s * p.num_heads + (long long)kvh * G + h0 + hh) * D + dd] =
+            Elem<T>::from_f(lt > 0.f ? a / lt : 0.f);
+    }
+}
+
+// ============================================================ host side
+namespace {
+
+template <typename T, int D, int NT, int NSTAGE>
+cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensorMap& tv,
+                        int grid, cudaStream_t st) {
+    using L = TcLayout<D, NT, NSTAGE>;
+    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE>;
+    static std::once_flag once[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static cudaError_t attr_err[64];
+    std::call_once(once[dev & 63], [&] {
+        attr_err[dev & 63] =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    });
+    if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
+    kern<<<grid, (kConsumerWarps + 1) * 32, L::kAlloc, st>>>(tk, tv, p);
+    return cudaGetLastError();
+}
+
+template <typename T, int D, int NT, int NSTAGE>
+int occupancy_t() {
+    using L = TcLayout<D, NT, NSTAGE>;
+    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) !=
+        cudaSuccess)
+        return 0;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kConsumerWarps + 1) * 32,
+                                                      L::kAlloc) != cudaSuccess)
+        return 0;
+    return n;
+}
+
+// Pipeline depth per head size: two CTAs per SM, each with this many
+// 64-token stages in flight.
+constexpr int kStages64 = 4;
+constexpr int kStages128 = 2;
+
+template <typename T>
+cudaError_t dispatch_tc(int head_dim, int group, const TcParams& p, const CUtensorMap& tk,
+                        const CUtensorMap& tv, int grid, cudaStream_t st) {
+    const bool two = group > 8;
+    if (head_dim == 64)
+        return two ? launch_tc_t<T, 64, 2, kStages64>(p, tk, tv, grid, st)
+                   : launch_tc_t<T, 64, 1, kStages64>(p, tk, tv, grid, st);
+    return two ? launch_tc_t<T, 128, 2, kStages128>(p, tk, tv, grid, st)
+               : launch_tc_t<T, 128, 1, kStages128>(p, tk, tv, grid, st);
+}
+
+template <typename T>
+int occupancy_dispatch(int head_dim, int group) {
+    const bool two = group > 8;
+    if (head_dim == 64)
+        return two ? occupancy_t<T, 64, 2, kStages64>() : occupancy_t<T, 64, 1, kStages64>();
+    return two ? occupancy_t<T, 128, 2, kStages128>() : occupancy_t<T, 128, 1, kStages128>();
+}
+
+template <typename T, int NPL>
+cudaError_t launch_generic_npl(const GenericParams& p, cudaStream_t st) {
+    constexpr int HG = NPL >= 32 ? 1 : 32 / NPL;
+    const size_t smem = (size_t)(HG * 32 * NPL + 8 * HG * 32 * NPL + 16 * HG) * sizeof(float);
+    auto kern = paged_attention_generic_kernel<T, NPL, HG>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.num_seqs, p.num_kv_heads, (p.group + HG - 1) / HG);
+    kern<<<grid, 256, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_generic_t(const GenericParams& p, cudaStream_t st) {
+    const int D = p.head_dim;
+    if (D <= 32) return launch_generic_npl<T, 1>(p, st);
+    if (D <= 64) return launch_generic_npl<T, 2>(p, st);
+    if (D <= 128) return launch_generic_npl<T, 4>(p, st);
+    if (D <= 256) return launch_generic_npl<T, 8>(p, st);
+    if (D <= 512) return launch_generic_npl<T, 16>(p, st);
+    return launch_generic_npl<T, 32>(p, st);
+}
+
+}  // namespace
+
+bool tc_supported(int dtype, int head_dim, int group, int block_size) {
+    if (dtype != TLB_FLOAT16 && dtype != TLB_BFLOAT16) return false;
+    if (head_dim != 64 && head_dim != 128) return false;
+    if (group < 1 || group > kGMax) return false;
+    if (block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64) return false;
+    return true;
+}
+
+int tc_gpad(int group) { return group > 8 ? 16 : 8; }
+
+int tc_grid(int device, int dtype, int head_dim, int group, cudaError_t* err) {
+    static std::mutex mu;
+    static int cache[64][2][2][2];  // device x dtype x head_dim x two-tiles
+    const int di = dtype == TLB_BFLOAT16 ? 1 : 0, hi = head_dim == 128 ? 1 : 0,
+              ti = group > 8 ? 1 : 0;
+    std::lock_guard<std::mutex> lk(mu);
+    int& c = cache[device & 63][di][hi][ti];
+    *err = cudaSuccess;
+    if (c == 0) {
+        int sms = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess) { *err = e; return 0; }
+        int occ = dtype == TLB_BFLOAT16 ? occupancy_dispatch<__nv_bfloat16>(head_dim, group)
+                                        : occupancy_dispatch<__half>(head_dim, group);
+        if (occ <= 0) { *err = cudaErrorInvalidConfiguration; return 0; }
+        if (occ > kMaxCtasPerSm) occ = kMaxCtasPerSm;
+        c = sms * occ;
+    }
+    return c;
+}
+
+cudaError_t launch_tc(int dtype, int head_dim, int group, const TcParams& p,
+                      const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid,
+                      cudaStream_t stream) {
+    if (dtype == TLB_BFLOAT16)
+        return dispatch_tc<__nv_bfloat16>(head_dim, group, p, tm_k, tm_v, grid, stream);
+    return dispatch_tc<__half>(head_dim, group, p, tm_k, tm_v, grid, stream);
+}
+
+cudaError_t launch_generic(int dtype, const GenericParams& p, cudaStream_t stream) {
+    switch (dtype) {
+        case TLB_FLOAT32: return launch_generic_t<float>(p, stream);
+        case TLB_FLOAT16: return launch_generic_t<__half>(p, stream);
+        default: return launch_generic_t<__nv_bfloat16>(p, stream);
+    }
+}
+
+}  // namespace attn
+}  // namespace tlb
