@@ -188,7 +188,7 @@ def run_ours(args, rank, world, local):
 
     from cscr import attention as A
     from cscr import pos_encoding as PE
-    from oracle import decode_oracle as O
+    from paged_decode import roofline as R
     from paged_decode import workloads as W
 
     dev = torch.device("cuda", local)
@@ -276,8 +276,8 @@ def run_ours(args, rank, world, local):
     value = tokens_per_step * steps / (step_ms / 1e3)
     lens_all = [b.seq_lens.cpu().numpy() for b in layers]
     attn_bytes = statistics.fmean(
-        O.attention_bytes(l, spec0.block_size, H, KVH, D, 2) for l in lens_all)
-    rope_bytes = O.rope_bytes(S, H, KVH, D, D, 2) + O.cache_write_bytes(S, KVH, D, 2)
+        R.attention_bytes(l, spec0.block_size, H, KVH, D, 2) for l in lens_all)
+    rope_bytes = R.rope_bytes(S, H, KVH, D, D, 2) + R.cache_write_bytes(S, KVH, D, 2)
     t_attn_us = attn_ms * 1e3 / steps
     t_step_us = step_ms * 1e3 / steps
     achieved = attn_bytes / (t_attn_us * 1e-6) / 1e9

@@ -265,30 +265,6 @@ def swap_blocks(src, dst, block_mapping):
         dst[d] = src[s]
 
 
-# ------------------------------------------------------------ accounting
-def attention_bytes(seq_lens, block_size, num_heads, num_kv_heads, head_dim, elem_bytes):
-    """Algorithmic bytes of one attention launch.
-
-    KV read 2*L*KVH*D*e per sequence + query read and output write
-    2*S*H*D*e + block-table entries 4*ceil(L/bs) + seq_lens 4*S.
-    """
-    L = np.clip(np.asarray(seq_lens, np.int64), 0, None)
-    S = L.shape[0]
-    kv = int((2 * L * num_kv_heads * head_dim * elem_bytes).sum())
-    qo = 2 * S * num_heads * head_dim * elem_bytes
-    tables = int((4 * np.ceil(L / block_size)).sum()) + 4 * S
-    return kv + qo + tables
-
-
-def rope_bytes(num_tokens, num_heads, num_kv_heads, head_dim, rot_dim, elem_bytes, pos_bytes=8):
-    return (2 * num_tokens * (num_heads + num_kv_heads) * head_dim * elem_bytes
-            + num_tokens * rot_dim * elem_bytes + num_tokens * pos_bytes)
-
-
-def cache_write_bytes(num_tokens, num_kv_heads, head_dim, elem_bytes):
-    return 2 * (2 * num_tokens * num_kv_heads * head_dim * elem_bytes) + 8 * num_tokens
-
-
 def ceil_div(a, b):
     return -(-a // b)
 
@@ -297,5 +273,5 @@ __all__ = [
     "DTYPES", "bf16_bits_to_f32", "f32_to_bf16_bits", "to_f32", "from_f32", "storage_np_dtype",
     "paged_attention", "paged_attention_threads", "rotary_embedding_neox", "cos_sin_cache",
     "write_kv_cache", "reshape_and_cache", "decode_metadata", "copy_blocks", "swap_blocks",
-    "attention_bytes", "rope_bytes", "cache_write_bytes", "ceil_div",
+    "ceil_div",
 ]
