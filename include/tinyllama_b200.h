@@ -90,11 +90,13 @@ TLB_API int tlb_get_device_status(uint32_t* status_out, int clear, void* stream)
  * whose length is <= 0, or whose blocks are all skipped, yields zeros.
  *
  * `workspace` is device scratch of at least the size that
- * tlb_paged_attention_workspace_size() returns for the same arguments. Its
- * first tlb_paged_attention_workspace_zeroed_bytes() bytes must be zero
- * before the first call; every call leaves them zero again, so one
- * zero-initialised buffer can be reused by successive calls on one stream.
- * Calls that overlap in time must use different workspaces.
+ * tlb_paged_attention_workspace_size() returns for the same arguments
+ * (256-byte aligned). Its first tlb_paged_attention_workspace_zeroed_bytes()
+ * bytes (arrival counters) must be zero when the call starts; the call
+ * leaves exactly that prefix zero again and writes partial results after it.
+ * Successive calls on one stream can therefore share a buffer, re-zeroing
+ * only when a call's prefix is longer than the previous call's (more
+ * sequences * kv heads). Calls that overlap in time need separate buffers.
  * ---------------------------------------------------------------------- */
 TLB_API int tlb_paged_attention_workspace_size(int64_t num_seqs, int64_t num_heads,
                                        int64_t num_kv_heads, int64_t head_dim,

@@ -191,6 +191,15 @@ def test_many_short_sequences(built_lib):
     check_attention(batch, out, seqs=list(range(0, 2000, 97)))
 
 
+def test_workspace_reuse_across_growing_batches(built_lib):
+    """Small batches dirty the scratch that a later, larger batch uses for its
+    arrival counters; the op must re-zero that prefix before the larger call."""
+    for S in (1, 3, 40, 600, 5, 1200):
+        batch = _custom_batch([700 + 37 * i for i in range(S)], 14, 2, 64, 16, "bfloat16")
+        out = _attend(batch)
+        check_attention(batch, out, seqs=sorted({0, S // 2, S - 1}))
+
+
 def test_two_streams_use_separate_workspaces(built_lib):
     b1 = W.make_batch(W.qwen3b_decode(1, batch=16))
     b2 = W.make_batch(W.qwen3b_decode(2, batch=16))

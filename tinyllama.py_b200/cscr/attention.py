@@ -18,35 +18,57 @@ from ._lib import DTYPE_CODE, torch_check
 
 _FLOAT_TYPES = (torch.float16, torch.bfloat16, torch.float32)
 
-# (device index, stream handle) -> zero-initialised uint8 workspace tensor.
-_workspaces: dict[tuple[int, int], torch.Tensor] = {}
-_ws_sizes: dict[tuple, int] = {}
+class _Workspace:
+    """Scratch of one (device, stream) and the length of its zero-at-rest prefix.
+
+    The kernel needs the arrival-counter prefix of the workspace to be zero
+    when it starts and leaves exactly that prefix zero when it ends; the bytes
+    after it hold partial results. A call whose counter prefix is longer than
+    the one currently known to be clean therefore zeroes it first (an async
+    memset on the same stream); calls of a steady shape never do.
+    """
+
+    __slots__ = ("buf", "clean")
+
+    def __init__(self, buf: torch.Tensor):
+        self.buf = buf
+        self.clean = buf.numel()
+
+
+# (device index, stream handle) -> workspace
+_workspaces: dict[tuple[int, int], _Workspace] = {}
+_ws_sizes: dict[tuple, tuple[int, int]] = {}
 
 
 def workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
-                    dtype: torch.dtype, device_index: int) -> int:
-    """Bytes of scratch the attention kernel needs for this shape on this device."""
+                    dtype: torch.dtype, device_index: int) -> tuple[int, int]:
+    """(total bytes, zero-at-rest prefix bytes) of scratch for this shape on this device."""
     key = (num_seqs, num_heads, num_kv_heads, head_dim, dtype, device_index)
     n = _ws_sizes.get(key)
     if n is None:
-        out = ctypes.c_size_t(0)
-        _lib.check(_lib.load().tlb_paged_attention_workspace_size(
-            num_seqs, num_heads, num_kv_heads, head_dim, DTYPE_CODE[dtype], ctypes.byref(out)))
-        n = out.value
+        lib = _lib.load()
+        total, zeroed = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.check(lib.tlb_paged_attention_workspace_size(
+            num_seqs, num_heads, num_kv_heads, head_dim, DTYPE_CODE[dtype], ctypes.byref(total)))
+        _lib.check(lib.tlb_paged_attention_workspace_zeroed_bytes(
+            num_seqs, num_kv_heads, ctypes.byref(zeroed)))
+        n = (total.value, zeroed.value)
         _ws_sizes[key] = n
     return n
 
 
-def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
+def _workspace(device: torch.device, stream: int, nbytes: int, zeroed: int) -> torch.Tensor | None:
     if nbytes == 0:
         return None
     key = (device.index, stream)
     ws = _workspaces.get(key)
-    if ws is None or ws.numel() < nbytes:
-        # Zeroed once: the kernel leaves its arrival counters at zero again.
-        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+    if ws is None or ws.buf.numel() < nbytes:
+        ws = _Workspace(torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device))
         _workspaces[key] = ws
-    return ws
+    if zeroed > ws.clean:
+        ws.buf[:zeroed].zero_()
+    ws.clean = zeroed
+    return ws.buf
 
 
 def paged_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
@@ -102,9 +124,9 @@ def paged_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: t
     lib = _lib.load()
     with _lib.device_guard(dev):
         stream = _lib.stream_of(dev)
-        nbytes = workspace_bytes(num_seqs, num_heads, num_kv_heads, head_dim, query.dtype,
-                                 dev.index)
-        ws = _workspace(dev, stream, nbytes)
+        nbytes, zeroed = workspace_bytes(num_seqs, num_heads, num_kv_heads, head_dim,
+                                         query.dtype, dev.index)
+        ws = _workspace(dev, stream, nbytes, zeroed)
         rc = lib.tlb_paged_attention(
             out.data_ptr(), query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
             block_tables.data_ptr(), seq_lens.data_ptr(), num_seqs, num_heads, num_kv_heads,
