@@ -47,7 +47,7 @@ import torch  # noqa: E402
 METRIC = "decode-attention tokens/sec and HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 UNIT = "tokens/s"
 WORKLOAD = "qwen2.5-3b decode step: 64 seqs/GPU, ctx U[128,4096], 16q/2kv heads, hd128, bs16, bf16"
-LAYERS = 4           # rotating independent KV pools
+LAYERS = 4           # default number of rotating independent KV pools
 FALLBACK_HBM_GBS = 6650.0
 NOMINAL_HBM_GBS = 8000.0
 
@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample budget (rank 0, N=1)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="rotating independent KV pools per GPU (profiling runs use 1)")
     return ap.parse_args()
 
 
@@ -201,7 +203,8 @@ def run_ours(args, rank, world, local):
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    layers = [W.make_batch(rank_spec(rank, world, args.seed, l), device=dev) for l in range(LAYERS)]
+    nl = args.layers
+    layers = [W.make_batch(rank_spec(rank, world, args.seed, l), device=dev) for l in range(nl)]
     spec0 = layers[0].spec
     S, H, KVH, D = len(spec0.seq_lens), spec0.num_heads, spec0.num_kv_heads, spec0.head_dim
     stream = torch.cuda.Stream(dev)
@@ -232,9 +235,9 @@ def run_ours(args, rank, world, local):
             for b in layers:
                 attn_only(b)
 
-    reps = max(1, args.steps // LAYERS)
-    steps = reps * LAYERS
-    wreps = max(1, math.ceil(args.warmup / LAYERS))
+    reps = max(1, args.steps // nl)
+    steps = reps * nl
+    wreps = max(1, math.ceil(args.warmup / nl))
 
     def timed(graph, n):
         with torch.cuda.stream(stream):
@@ -291,13 +294,13 @@ def run_ours(args, rank, world, local):
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
-        "steps": steps, "warmup": wreps * LAYERS, "ms_per_step": round(step_ms / steps, 6),
+        "steps": steps, "warmup": wreps * nl, "ms_per_step": round(step_ms / steps, 6),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v and KV pool, seeded lengths)",
         "config": {"workload": WORKLOAD, "global_batch": tokens_per_step, "seq_len": "U[128,4096]",
                    "parallelism": f"sequence-sharded x{world} (LPT), no collective",
-                   "l2": f"{LAYERS} rotating independent KV pools per GPU "
-                         f"(~{LAYERS * attn_bytes / 1e6:.0f} MB of KV per rotation > 126 MB L2)",
+                   "l2": f"{nl} rotating independent KV pools per GPU "
+                         f"(~{nl * attn_bytes / 1e6:.0f} MB of KV per rotation > 126 MB L2)",
                    "timed_region": "CUDA-graph replay of fused RoPE+cache-write + paged attention"},
         "hbm_gbs_step": round((attn_bytes + rope_bytes) / (t_step_us * 1e-6) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round((attn_bytes + rope_bytes) / (t_step_us * 1e-6) / 1e9
@@ -371,8 +374,10 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
         hosts.append(h); devs.append(d); views.append(v)
         outs.append(torch.empty(S, H, D, dtype=torch.bfloat16).pin_memory())
 
+    nl = len(layers)
+
     def one(i):
-        r = i % LAYERS
+        r = i % nl
         b, v = layers[r], views[r]
         devs[r].copy_(hosts[r], non_blocking=True)
         q_rot = PE.rotary_embedding_neox_with_cache(v["positions"], v["query"], v["key"],
@@ -382,9 +387,9 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
                                 v["lens"], b.scale)
         outs[r].copy_(out, non_blocking=True)
 
-    steps = max(LAYERS, (args.steps // 4) // LAYERS * LAYERS)
+    steps = max(nl, (args.steps // 4) // nl * nl)
     with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, LAYERS)):
+        for i in range(max(args.warmup, nl)):
             one(i)
         stream.synchronize()
         barrier()

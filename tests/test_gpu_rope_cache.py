@@ -43,9 +43,13 @@ def _check_rope(q, k, pos, cs, hs, dtype, out, k_after):
     tol = tol_for(dtype)
     np.testing.assert_allclose(O.to_f32(W.to_numpy(out), dtype), O.to_f32(ref_out, dtype), **tol)
     np.testing.assert_allclose(O.to_f32(W.to_numpy(k_after), dtype), O.to_f32(ref_k, dtype), **tol)
-    # fp32 math rounded once: nearly every element is bit-identical to the oracle
-    same = (W.to_numpy(out) == ref_out).mean()
-    assert same > 0.99, same
+    if dtype != "float32":
+        # fp32 math rounded once to 16 bits: nearly every element is bit-identical
+        # (fused multiply-add vs separate products only moves the last fp32 bit)
+        same = (W.to_numpy(out) == ref_out).mean()
+        assert same > 0.99, same
+    else:
+        np.testing.assert_allclose(W.to_numpy(out), ref_out, rtol=3e-7, atol=1e-6)
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])

@@ -90,8 +90,8 @@ def rotary_embedding_neox_with_cache(postions: torch.Tensor, query: torch.Tensor
     """
     out = torch.empty_like(query)
     num_tokens, rot_dim = _check_rope(postions, query, key, head_size, cos_sin_cache, out)
-    torch_check(value.is_cuda and key_cache.is_cuda and value_cache.is_cuda
-                and slot_mapping.is_cuda, "value, caches and slot_mapping must be CUDA tensors")
+    torch_check(value.is_cuda and key_cache.is_cuda and value_cache.is_cuda,
+                "value and caches must be CUDA tensors")
     torch_check(key_cache.dim() == 4 and value_cache.shape == key_cache.shape,
                 "key_cache and value_cache must be [num_blocks, num_kv_heads, block_size, head_size]")
     torch_check(key_cache.is_contiguous() and value_cache.is_contiguous(),

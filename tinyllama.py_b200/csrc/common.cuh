@@ -46,6 +46,26 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Probabilities in [0, 1] as mma operands: fp16 keeps 11 significant bits,
+// which is enough; bf16 keeps 8, so it is carried as a hi + lo pair whose sum
+// holds 16 bits (lo is the bf16 rounding of the remainder).
+template <typename T> constexpr bool kSplitP = false;
+template <> constexpr bool kSplitP<__nv_bfloat16> = true;
+
+template <typename T>
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    if constexpr (kSplitP<T>) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        const float2 hf = __bfloat1622float2(h);
+        const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+        hi = *reinterpret_cast<const uint32_t*>(&h);
+        lo = *reinterpret_cast<const uint32_t*>(&l);
+    } else {
+        hi = pack2<T>(a, b);
+        lo = 0u;
+    }
+}
+
 // ------------------------------------------------------------- shared mem
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -536,11 +536,13 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 }
             }
             // P^T as the B operand: tokens (2q, 2q+1) and (8+2q, 8+2q+1) of head g.
-            uint32_t pb[NT][2];
+            // bf16 keeps 8 mantissa bits, so P goes in as hi + lo bf16 pairs
+            // (two mmas) and the weights match the fp32 row sums to ~2^-16.
+            uint32_t pb[NT][2], pl[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                pb[nt][0] = pack2<T>(pr[0][2 * nt], pr[0][2 * nt + 1]);
-                pb[nt][1] = pack2<T>(pr[1][2 * nt], pr[1][2 * nt + 1]);
+                split2<T>(pr[0][2 * nt], pr[0][2 * nt + 1], pb[nt][0], pl[nt][0]);
+                split2<T>(pr[1][2 * nt], pr[1][2 * nt + 1], pb[nt][1], pl[nt][1]);
             }
             // ---- O^T += V^T P^T, one 16-wide slice of head_dim per m-tile.
 #pragma unroll
@@ -553,7 +555,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 uint32_t a[4];
                 ldsm_x4_trans(addr, a[0], a[1], a[2], a[3]);
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) mma16816<T>(o[nt][mt], a, pb[nt][0], pb[nt][1]);
+                for (int nt = 0; nt < NT; ++nt) {
+                    mma16816<T>(o[nt][mt], a, pb[nt][0], pb[nt][1]);
+                    if constexpr (kSplitP<T>) mma16816<T>(o[nt][mt], a, pl[nt][0], pl[nt][1]);
+                }
             }
         }
         __syncwarp();
