@@ -216,7 +216,7 @@ def run_ours(args, rank, world, local):
                                                     b.value_cache, b.slot_mapping, D,
                                                     b.cos_sin_cache)
         return A.paged_attention(q_rot.view(S, H, D), b.key_cache, b.value_cache,
-                                 b.block_tables, b.seq_lens, b.scale)
+                                 b.block_tables, b.seq_lens, b.scale, overlap_prologue=True)
 
     def attn_only(b):
         return A.paged_attention(b.query, b.key_cache, b.value_cache, b.block_tables,
@@ -384,7 +384,7 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
                                                     v["value"], b.key_cache, b.value_cache,
                                                     v["slots"], D, b.cos_sin_cache)
         out = A.paged_attention(q_rot.view(S, H, D), b.key_cache, b.value_cache, v["tables"],
-                                v["lens"], b.scale)
+                                v["lens"], b.scale, overlap_prologue=True)
         outs[r].copy_(out, non_blocking=True)
 
     steps = max(nl, (args.steps // 4) // nl * nl)

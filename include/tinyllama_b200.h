@@ -106,6 +106,14 @@ TLB_API int tlb_paged_attention_workspace_zeroed_bytes(int64_t num_seqs,
                                                int64_t num_kv_heads,
                                                size_t* bytes_out);
 
+/* Flags of tlb_paged_attention. */
+/* The kernel launched just before on `stream` writes neither block_tables
+ * nor seq_lens (nor reads the output buffer): the attention kernel may then
+ * start while that kernel finishes and read this metadata early
+ * (programmatic dependent launch); query and cache are still read only after
+ * it completes. Leave unset when the predecessor is unknown. */
+#define TLB_ATTN_OVERLAP_PROLOGUE 0x1u
+
 TLB_API int tlb_paged_attention(void* out, const void* query, const void* key_cache,
                         const void* value_cache, const int32_t* block_tables,
                         const int32_t* seq_lens, int64_t num_seqs,
@@ -113,7 +121,7 @@ TLB_API int tlb_paged_attention(void* out, const void* query, const void* key_ca
                         int64_t head_dim, int64_t num_blocks,
                         int64_t block_size, int64_t max_blocks_per_seq,
                         float scale, int dtype, void* workspace,
-                        size_t workspace_bytes, void* stream);
+                        size_t workspace_bytes, unsigned flags, void* stream);
 
 /* ------------------------------------------------------------------------
  * NeoX rotary embedding.

@@ -46,13 +46,13 @@ def test_argument_errors_without_gpu(built_lib):
     from cscr import _lib
 
     lib = _lib.load()
-    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 0, 16, 2, 128, 10, 16, 4, 1.0, 2, None, 0, None)
+    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 0, 16, 2, 128, 10, 16, 4, 1.0, 2, None, 0, 0, None)
     assert rc == 1 and "at least one sequence" in _lib.last_error()
-    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 4, 15, 2, 128, 10, 16, 4, 1.0, 2, None, 0, None)
+    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 4, 15, 2, 128, 10, 16, 4, 1.0, 2, None, 0, 0, None)
     assert rc == 1 and "divisible" in _lib.last_error()
-    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 4, 16, 2, 2048, 10, 16, 4, 1.0, 2, None, 0, None)
+    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 4, 16, 2, 2048, 10, 16, 4, 1.0, 2, None, 0, 0, None)
     assert rc == 1 and "head_dim too large" in _lib.last_error()
-    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 4, 16, 2, 128, 10, 16, 4, 1.0, 7, None, 0, None)
+    rc = lib.tlb_paged_attention(1, 1, 1, 1, 1, 1, 4, 16, 2, 128, 10, 16, 4, 1.0, 7, None, 0, 0, None)
     assert rc == 1 and "dtype" in _lib.last_error()
     rc = lib.tlb_rotary_embedding_neox(1, 1, 4, 1, 1, 4, 2, 1, 64, 1, 10, 63, 128, 64, 128, 2, None)
     assert rc == 1 and "even" in _lib.last_error()

@@ -73,12 +73,17 @@ def _workspace(device: torch.device, stream: int, nbytes: int, zeroed: int) -> t
 
 def paged_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                     block_tables: torch.Tensor, seq_lens: torch.Tensor,
-                    scale: float) -> torch.Tensor:
+                    scale: float, *, overlap_prologue: bool = False) -> torch.Tensor:
     """PagedAttention decode forward (CUDA, sm_100a).
 
     query [num_seqs, num_heads, head_dim]; key_cache / value_cache
     [num_blocks, num_kv_heads, block_size, head_dim]; block_tables
     [num_seqs, max_blocks_per_seq] int32; seq_lens [num_seqs] int32.
+
+    ``overlap_prologue`` (keyword only, not in the reference API) lets the
+    kernel start while the kernel launched just before it on this stream is
+    finishing; set it only when that kernel writes neither block_tables nor
+    seq_lens — e.g. right after ``rotary_embedding_neox_with_cache``.
     """
     torch_check(query.is_cuda, "query must be a CUDA tensor")
     torch_check(key_cache.is_cuda, "key_cache must be a CUDA tensor")
@@ -132,6 +137,6 @@ def paged_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: t
             block_tables.data_ptr(), seq_lens.data_ptr(), num_seqs, num_heads, num_kv_heads,
             head_dim, num_blocks, block_size, block_tables.size(1), float(scale),
             DTYPE_CODE[query.dtype], ws.data_ptr() if ws is not None else None,
-            ws.numel() if ws is not None else 0, stream)
+            ws.numel() if ws is not None else 0, 1 if overlap_prologue else 0, stream)
         _lib.check(rc)
     return out

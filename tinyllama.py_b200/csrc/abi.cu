@@ -206,7 +206,8 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
                         const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
                         int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
                         int64_t block_size, int64_t max_blocks_per_seq, float scale, int dtype,
-                        void* workspace, size_t workspace_bytes, void* stream) {
+                        void* workspace, size_t workspace_bytes, unsigned flags,
+                        void* stream) {
     TLB_REQUIRE(is_float(dtype), "dtype must be float16, bfloat16 or float32");
     TLB_REQUIRE(num_seqs > 0, "query must contain at least one sequence");
     TLB_REQUIRE(num_heads > 0 && num_kv_heads > 0 && head_dim > 0 && num_blocks > 0 &&
@@ -263,7 +264,8 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
         p.max_blocks = (int)max_blocks_per_seq;
         p.min_units = (int)(512 / block_size) > 0 ? (int)(512 / block_size) : 1;
         p.scale_log2 = scale_log2;
-        e = tlb::attn::launch_tc(dtype, (int)head_dim, group, p, tk, tv, grid, st);
+        e = tlb::attn::launch_tc(dtype, (int)head_dim, group, p, tk, tv, grid,
+                                 (flags & TLB_ATTN_OVERLAP_PROLOGUE) != 0, st);
         if (e != cudaSuccess) return cuda_fail(e, "launching paged attention");
         return TLB_OK;
     }

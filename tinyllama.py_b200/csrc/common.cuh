@@ -182,6 +182,27 @@ __device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// atomicInc with release-acquire semantics at GPU scope:
+// *p = (*p >= limit) ? 0 : *p + 1, returns the old value.
+__device__ __forceinline__ unsigned atomic_inc_acq_rel(unsigned* p, unsigned limit) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "l"(p), "r"(limit)
+                 : "memory");
+    return old;
+}
+
+// Programmatic dependent launch: wait until the kernel this one was allowed
+// to overlap has finished and its writes are visible (no-op otherwise), and
+// let the next kernel's prologue start early.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named barrier among `count` threads (count a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

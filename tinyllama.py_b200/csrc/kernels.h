@@ -14,7 +14,7 @@ constexpr int kConsumerWarps = 4;   // warps that run the mma / softmax
 constexpr int kTileRows = 16;       // tokens per warp tile (mma k / n extent)
 constexpr int kStageRows = kConsumerWarps * kTileRows;  // tokens per pipeline stage
 constexpr int kGMax = 16;           // largest query-head group on the tensor-core path
-constexpr int kMaxCtasPerSm = 2;    // bound used to size the partial-result workspace
+constexpr int kMaxCtasPerSm = 1;    // persistent: one CTA per SM (sizes the workspace too)
 constexpr int kWorkspaceHeader = 256;
 
 struct TcParams {
@@ -61,8 +61,10 @@ int tc_gpad(int group);
 // Number of CTAs the tensor-core kernel launches on `device` (persistent grid).
 int tc_grid(int device, int dtype, int head_dim, int group, cudaError_t* err);
 
+// `overlap`: launch with programmatic stream serialization (the kernel reads
+// metadata before griddepcontrol.wait; see TLB_ATTN_OVERLAP_PROLOGUE).
 cudaError_t launch_tc(int dtype, int head_dim, int group, const TcParams& p,
-                      const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid,
+                      const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid, bool overlap,
                       cudaStream_t stream);
 cudaError_t launch_generic(int dtype, const GenericParams& p, cudaStream_t stream);
 

@@ -66,7 +66,7 @@ struct TcLayout {
     static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
     static constexpr int kChunkBytes = kStageRows * 128;
     static constexpr int kStageKV = kStageRows * D * 2;  // bytes of K (or V) per stage
-    static constexpr int kQBytes = kGMax * D * 2;
+    static constexpr int kQBytes = 8 * NT * D * 2;     // query group of the piece
     static constexpr int kGP = 8 * NT;                 // padded heads per piece
     static constexpr int kOFloats = kConsumerWarps * kGP * D;
     static constexpr int kOffK = 0;
@@ -184,27 +184,41 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
     long long total_blocks;
     block_incl_scan(my_blocks, sScan, &total_blocks);
 
+    // Until griddepcontrol.wait this kernel only reads metadata (seq_lens,
+    // block_tables) and writes nothing: with programmatic launch it may be
+    // running beside the kernel before it.
     T* out = reinterpret_cast<T*>(p.out);
-    for (int s = blockIdx.x; s < S; s += gridDim.x) {
-        if (p.seq_lens[s] <= 0) {
-            const long long base = (long long)s * p.num_heads * D;
-            for (int e = tid; e < p.num_heads * D; e += blockDim.x)
-                out[base + e] = Elem<T>::from_f(0.f);
+    // Sequences with no context get zeros (attention_kernel.cu:102); CTA j
+    // covers sequences j, j + grid, ... with the threads [first, first + n).
+    auto zero_empty_outputs = [&](int first, int n) {
+        for (int s = blockIdx.x; s < S; s += gridDim.x) {
+            if (p.seq_lens[s] <= 0) {
+                const long long base = (long long)s * p.num_heads * D;
+                for (int e = first; e < p.num_heads * D; e += n)
+                    out[base + e] = Elem<T>::from_f(0.f);
+            }
         }
-    }
+    };
 
     const long long W = total_blocks * KVH;
-    if (W == 0) return;
+    if (W == 0) {
+        grid_dependency_wait();
+        zero_empty_outputs(tid, blockDim.x);
+        return;
+    }
     int P = (int)gridDim.x;
     {
         const long long want = (W + p.min_units - 1) / p.min_units;
         if (want < P) P = (int)(want > 0 ? want : 1);
     }
     const int j = blockIdx.x;
-    if (j >= P) return;
+    if (j >= P) {
+        grid_dependency_wait();
+        zero_empty_outputs(tid, blockDim.x);
+        return;
+    }
     const long long ustart = range_start(j, W, P);
     const long long uend = range_start(j + 1, W, P);
-    if (ustart >= uend) return;
 
     // ---- pass 2: locate the sequence holding unit `ustart`.
     if (tid == 0) sMisc[0] = -1;
@@ -233,7 +247,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
     __syncthreads();
     const int s_first = sMisc[0];
     const long long pre_first = reinterpret_cast<long long*>(sMisc)[1];
-    if (s_first < 0) return;  // cannot happen for ustart < W; never walk from garbage
+    if (s_first < 0) {  // cannot happen for ustart < W; never walk from garbage
+        grid_dependency_wait();
+        zero_empty_outputs(tid, blockDim.x);
+        return;
+    }
 
     if (warp == kConsumerWarps) {
         // ===================================================== producer warp
@@ -289,6 +307,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         int bid = -1;
         if (job.valid && lane < job.nblk)
             bid = p.block_tables[(long long)job.s * p.max_blocks + job.cb + lane];
+        // Everything above reads only metadata; the query and the cache may
+        // still be written by the kernel launched just before this one.
+        grid_dependency_wait();
+        zero_empty_outputs(lane, 32);
         int stage = 0;
         uint32_t phase = 0;
         bool first_piece = true;
@@ -625,16 +647,18 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             }
         }
         if (!complete) {
-            __threadfence();
+            // The barrier orders every consumer thread's partial stores before
+            // thread 0's release-acquire increment (cumulativity), and the
+            // acquire side orders the other pieces' stores before the reads
+            // of the CTA that arrives last.
             named_bar_sync(1, kConsumerThreads);
             if (tid == 0) {
-                const unsigned old = atomicInc(p.counters + d.u, (unsigned)(d.nsplits - 1));
+                const unsigned old = atomic_inc_acq_rel(p.counters + d.u, (unsigned)(d.nsplits - 1));
                 sMisc[8] = old == (unsigned)(d.nsplits - 1) ? 1 : 0;
             }
             named_bar_sync(1, kConsumerThreads);
             if (sMisc[8]) {
                 // Last piece of this (sequence, kv head) to finish: merge all.
-                __threadfence();
                 const int n = d.nsplits;
                 const int cap = L::kOFloats / 2;  // floats for maxima, same for sums
                 float* wM = sO;
@@ -821,7 +845,7 @@ namespace {
 
 template <typename T, int D, int NT, int NSTAGE>
 cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensorMap& tv,
-                        int grid, cudaStream_t st) {
+                        int grid, bool overlap, cudaStream_t st) {
     using L = TcLayout<D, NT, NSTAGE>;
     auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE>;
     static std::once_flag once[64];
@@ -834,8 +858,17 @@ cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensor
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     });
     if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
-    kern<<<grid, (kConsumerWarps + 1) * 32, L::kAlloc, st>>>(tk, tv, p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3((kConsumerWarps + 1) * 32);
+    cfg.dynamicSmemBytes = L::kAlloc;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = overlap ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
 }
 
 template <typename T, int D, int NT, int NSTAGE>
@@ -852,20 +885,21 @@ int occupancy_t() {
     return n;
 }
 
-// Pipeline depth per head size: two CTAs per SM, each with this many
-// 64-token stages in flight.
-constexpr int kStages64 = 4;
-constexpr int kStages128 = 2;
+// Pipeline depth per head size: one CTA per SM keeps this many 64-token
+// stages (K, V and the query group) in flight, ~160 KB per SM, enough to
+// cover HBM latency under full load (bytes in flight = bandwidth x latency).
+constexpr int kStages64 = 10;
+constexpr int kStages128 = 5;
 
 template <typename T>
 cudaError_t dispatch_tc(int head_dim, int group, const TcParams& p, const CUtensorMap& tk,
-                        const CUtensorMap& tv, int grid, cudaStream_t st) {
+                        const CUtensorMap& tv, int grid, bool ov, cudaStream_t st) {
     const bool two = group > 8;
     if (head_dim == 64)
-        return two ? launch_tc_t<T, 64, 2, kStages64>(p, tk, tv, grid, st)
-                   : launch_tc_t<T, 64, 1, kStages64>(p, tk, tv, grid, st);
-    return two ? launch_tc_t<T, 128, 2, kStages128>(p, tk, tv, grid, st)
-               : launch_tc_t<T, 128, 1, kStages128>(p, tk, tv, grid, st);
+        return two ? launch_tc_t<T, 64, 2, kStages64>(p, tk, tv, grid, ov, st)
+                   : launch_tc_t<T, 64, 1, kStages64>(p, tk, tv, grid, ov, st);
+    return two ? launch_tc_t<T, 128, 2, kStages128>(p, tk, tv, grid, ov, st)
+               : launch_tc_t<T, 128, 1, kStages128>(p, tk, tv, grid, ov, st);
 }
 
 template <typename T>
@@ -933,11 +967,11 @@ int tc_grid(int device, int dtype, int head_dim, int group, cudaError_t* err) {
 }
 
 cudaError_t launch_tc(int dtype, int head_dim, int group, const TcParams& p,
-                      const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid,
+                      const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid, bool overlap,
                       cudaStream_t stream) {
     if (dtype == TLB_BFLOAT16)
-        return dispatch_tc<__nv_bfloat16>(head_dim, group, p, tm_k, tm_v, grid, stream);
-    return dispatch_tc<__half>(head_dim, group, p, tm_k, tm_v, grid, stream);
+        return dispatch_tc<__nv_bfloat16>(head_dim, group, p, tm_k, tm_v, grid, overlap, stream);
+    return dispatch_tc<__half>(head_dim, group, p, tm_k, tm_v, grid, overlap, stream);
 }
 
 cudaError_t launch_generic(int dtype, const GenericParams& p, cudaStream_t stream) {

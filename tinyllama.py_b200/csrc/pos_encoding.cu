@@ -125,6 +125,10 @@ __device__ __forceinline__ void rotate(const T* src, T* dst, const T* cs, int ha
 template <typename T, typename PI, typename SI, int VEC, bool WITH_QUERY, bool WITH_CACHE,
           bool BY_TABLE>
 __global__ void __launch_bounds__(256) rope_cache_kernel(const RopeCacheParams p) {
+    // A kernel launched after this one with programmatic serialization (the
+    // attention kernel) may start its metadata prologue now; it still waits
+    // for this grid to finish before reading anything written here.
+    grid_launch_dependents();
     const int half = p.rot_dim / 2;
     const int hv = half / VEC;                       // pair vectors per head
     const int pv = (p.head_size - p.rot_dim) / VEC;  // pass-through vectors per head

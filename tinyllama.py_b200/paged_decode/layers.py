@@ -90,7 +90,8 @@ class PagedAttentionWithRoPE(PagedAttention):
         cos_sin_cache = self._table(query.device, query.dtype)
         tables = block_tables if block_tables.dtype == torch.int32 else block_tables.to(torch.int32)
         tables = tables.contiguous()
-        if key_cache.dtype == query.dtype and value.dtype == query.dtype:
+        fused = key_cache.dtype == query.dtype and value.dtype == query.dtype
+        if fused:
             query_2d = _PE.rotary_embedding_neox_with_cache(
                 positions, query_2d, key_2d, value, key_cache, value_cache, None,
                 self.head_size, cos_sin_cache, block_tables=tables)
@@ -99,4 +100,8 @@ class PagedAttentionWithRoPE(PagedAttention):
                                                  cos_sin_cache)
             self._write_kv_cache(key_2d, value, positions, key_cache, value_cache, tables)
         query = query_2d.view(num_tokens, num_heads, head_size)
-        return super().forward(query, key_cache, value_cache, tables, seq_lens)
+        # The kernel just launched (RoPE + cache write) writes neither the
+        # block tables nor seq_lens, so attention may overlap its prologue.
+        return _C.paged_attention(query=query, key_cache=key_cache, value_cache=value_cache,
+                                  block_tables=tables, seq_lens=seq_lens, scale=self.scale,
+                                  overlap_prologue=fused)
