@@ -11,7 +11,7 @@
 #include <string>
 #include <unordered_map>
 
-#include "../../include/tinyllama_b200.h"
+#include "tinyllama_b200.h"
 #include "common.cuh"
 #include "kernels.h"
 

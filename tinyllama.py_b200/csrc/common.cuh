@@ -9,7 +9,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/tinyllama_b200.h"
+#include "tinyllama_b200.h"
 
 namespace tlb {
 
@@ -201,6 +201,21 @@ __device__ __forceinline__ void grid_dependency_wait() {
 }
 __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// 4-byte asynchronous global -> shared copy (Ampere-style cp.async), for
+// small metadata that must arrive ahead of its use.
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src))
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Named barrier among `count` threads (count a multiple of 32).

@@ -14,7 +14,11 @@ constexpr int kConsumerWarps = 4;   // warps that run the mma / softmax
 constexpr int kTileRows = 16;       // tokens per warp tile (mma k / n extent)
 constexpr int kStageRows = kConsumerWarps * kTileRows;  // tokens per pipeline stage
 constexpr int kGMax = 16;           // largest query-head group on the tensor-core path
-constexpr int kMaxCtasPerSm = 1;    // persistent: one CTA per SM (sizes the workspace too)
+#ifndef TLB_ATTN_CTAS_PER_SM
+#define TLB_ATTN_CTAS_PER_SM 1
+#endif
+// Persistent grid: at most this many CTAs per SM (also sizes the workspace).
+constexpr int kMaxCtasPerSm = TLB_ATTN_CTAS_PER_SM;
 constexpr int kWorkspaceHeader = 256;
 
 struct TcParams {

@@ -61,6 +61,21 @@ struct StageDesc {
     int u;           // sequence * num_kv_heads + kv head
 };
 
+constexpr int kSeqCache = 256;  // context lengths cached per CTA for the producer
+constexpr int kJobRing = 8;     // producer job ring (jobs generated ahead of issue)
+constexpr int kPrefetch = 6;    // stages whose block ids are in flight ahead of the issue
+
+// One stage job of the producer: a run of <= blocks_per_stage KV blocks of a
+// single (sequence, kv head) piece.
+struct alignas(8) Job {
+    int s, h, cb, nblk;
+    int nb;          // blocks of the sequence (clamped)
+    int seqlen;
+    int b_lo, b_hi;  // block range of the piece
+    long long pre;   // KV blocks of all sequences before s
+    bool valid;
+};
+
 template <int D, int NT, int NSTAGE>
 struct TcLayout {
     static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
@@ -79,7 +94,9 @@ struct TcLayout {
     static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
     static constexpr int kOffMisc = kOffBar + 2 * NSTAGE * 8;
     static constexpr int kMiscInts = 64;
-    static constexpr int kBytes = kOffMisc + kMiscInts * 4;
+    static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
+    static constexpr int kProdBytes = kSeqCache * 4 + kJobRing * (int)sizeof(Job) + kJobRing * 8 * 4;
+    static constexpr int kBytes = kOffProd + kProdBytes;
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
@@ -114,16 +131,7 @@ __device__ __forceinline__ long long range_start(int j, long long W, int P) {
     return (long long)j * W / P;
 }
 
-// One stage job of the producer: a run of <= blocks_per_stage KV blocks of a
-// single (sequence, kv head) piece.
-struct Job {
-    int s, h, cb, nblk;
-    int nb;          // blocks of the sequence (clamped)
-    int seqlen;
-    int b_lo, b_hi;  // block range of the piece
-    long long pre;   // KV blocks of all sequences before s
-    bool valid;
-};
+
 
 }  // namespace
 
@@ -253,15 +261,29 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         return;
     }
 
+    // Context lengths of the sequences this CTA starts with, cached for the
+    // producer's walk (metadata only: allowed before griddepcontrol.wait).
+    int* sSeqLen = reinterpret_cast<int*>(smem + L::kOffProd);
+    for (int i = tid; i < kSeqCache; i += blockDim.x) {
+        const int s = s_first + i;
+        sSeqLen[i] = s < S ? p.seq_lens[s] : 0;
+    }
+    __syncthreads();
+
     if (warp == kConsumerWarps) {
         // ===================================================== producer warp
         const int bps = kStageRows / bs;  // blocks per stage
         const uint64_t pol = l2_policy_evict_first();
         const int P_ = P;
         const T* query = reinterpret_cast<const T*>(p.query);
+        Job* sJob = reinterpret_cast<Job*>(smem + L::kOffProd + kSeqCache * 4);
+        const uint32_t sBid = sbase + L::kOffProd + kSeqCache * 4 + kJobRing * (int)sizeof(Job);
+        const int* sBidPtr = reinterpret_cast<const int*>(smem + L::kOffProd + kSeqCache * 4 +
+                                                          kJobRing * (int)sizeof(Job));
 
         auto seq_blocks = [&](int s, int& seqlen) -> int {
-            int len = min(p.seq_lens[s], cap_tokens);
+            int len = s - s_first < kSeqCache ? sSeqLen[s - s_first] : p.seq_lens[s];
+            len = min(len, cap_tokens);
             seqlen = len > 0 ? len : 0;
             return len > 0 ? (len + bs - 1) / bs : 0;
         };
@@ -303,10 +325,21 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             return piece_job(x, jb.s + 1, jb.pre + jb.nb);
         };
 
-        Job job = piece_job(ustart, s_first, pre_first);
-        int bid = -1;
-        if (job.valid && lane < job.nblk)
-            bid = p.block_tables[(long long)job.s * p.max_blocks + job.cb + lane];
+        // Jobs are generated kPrefetch stages ahead of the one being issued:
+        // the job goes to a shared ring and its block ids are copied there
+        // with cp.async, so the dependent global read of the block table
+        // never sits between two TMA issues.
+        Job pj = piece_job(ustart, s_first, pre_first);
+        auto prefetch = [&](int k) {
+            const int slot = k % kJobRing;
+            if (lane == 0) sJob[slot] = pj;
+            if (pj.valid && lane < pj.nblk)
+                cp_async_4(sBid + (uint32_t)(slot * 8 + lane) * 4u,
+                           p.block_tables + (long long)pj.s * p.max_blocks + pj.cb + lane);
+            cp_async_commit();
+            if (pj.valid) pj = next_job(pj);
+        };
+        for (int k = 0; k < kPrefetch; ++k) prefetch(k);
         // Everything above reads only metadata; the query and the cache may
         // still be written by the kernel launched just before this one.
         grid_dependency_wait();
@@ -315,11 +348,13 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         uint32_t phase = 0;
         bool first_piece = true;
         bool ok = true;
-        while (job.valid) {
-            const Job nxt = next_job(job);
-            int nbid = -1;
-            if (nxt.valid && lane < nxt.nblk)
-                nbid = p.block_tables[(long long)nxt.s * p.max_blocks + nxt.cb + lane];
+        for (int k = 0;; ++k) {
+            prefetch(k + kPrefetch);
+            cp_async_wait<kPrefetch>();  // job k and its block ids have landed
+            __syncwarp();
+            const Job job = sJob[k % kJobRing];
+            if (!job.valid) break;
+            const int bid = lane < job.nblk ? sBidPtr[(k % kJobRing) * 8 + lane] : -1;
 
             bool waited = true;
             if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
@@ -384,9 +419,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             }
             if (piece_end) first_piece = false;
             if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
-            job = nxt;
-            bid = nbid;
         }
+        cp_async_wait<0>();
         if (ok) {
             bool waited = true;
             if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
@@ -490,12 +524,14 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 __syncwarp();
             }
 
-            // ---- S = Q K^T for 16 tokens (two 8-token n-tiles).
-            float s_acc[2][4];
+            // ---- S = Q K^T for 16 tokens (two 8-token n-tiles). Even and odd
+            // k-steps accumulate separately: two independent mma chains of
+            // half the depth, summed at the end.
+            float s_acc[2][4], s_odd[2][4];
 #pragma unroll
             for (int n = 0; n < 2; ++n)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) s_acc[n][e] = 0.f;
+                for (int e = 0; e < 4; ++e) s_acc[n][e] = s_odd[n][e] = 0.f;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 const int c = ks >> 2;
@@ -505,9 +541,15 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                     kbase + c * L::kChunkBytes + row * 128 + ((kk ^ (row & 7)) << 4);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(addr, b0, b1, b2, b3);
-                mma16816<T>(s_acc[0], qa[ks], b0, b1);
-                mma16816<T>(s_acc[1], qa[ks], b2, b3);
+                float (&acc0)[4] = (ks & 1) ? s_odd[0] : s_acc[0];
+                float (&acc1)[4] = (ks & 1) ? s_odd[1] : s_acc[1];
+                mma16816<T>(acc0, qa[ks], b0, b1);
+                mma16816<T>(acc1, qa[ks], b2, b3);
             }
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s_acc[n][e] += s_odd[n][e];
 
             // ---- online softmax (log2 domain); heads g (and g + 8).
             float x[2][4];
@@ -888,8 +930,14 @@ int occupancy_t() {
 // Pipeline depth per head size: one CTA per SM keeps this many 64-token
 // stages (K, V and the query group) in flight, ~160 KB per SM, enough to
 // cover HBM latency under full load (bytes in flight = bandwidth x latency).
-constexpr int kStages64 = 10;
-constexpr int kStages128 = 5;
+#ifndef TLB_ATTN_STAGES_64
+#define TLB_ATTN_STAGES_64 10
+#endif
+#ifndef TLB_ATTN_STAGES_128
+#define TLB_ATTN_STAGES_128 5
+#endif
+constexpr int kStages64 = TLB_ATTN_STAGES_64;
+constexpr int kStages128 = TLB_ATTN_STAGES_128;
 
 template <typename T>
 cudaError_t dispatch_tc(int head_dim, int group, const TcParams& p, const CUtensorMap& tk,
