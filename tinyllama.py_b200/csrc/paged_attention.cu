@@ -61,7 +61,7 @@ struct StageDesc {
     int u;           // sequence * num_kv_heads + kv head
 };
 
-constexpr int kSeqCache = 256;  // context lengths cached per CTA for the producer
+constexpr int kSeqCache = 2048; // context lengths kept in shared memory (first 2048 seqs)
 constexpr int kJobRing = 8;     // producer job ring (jobs generated ahead of issue)
 constexpr int kPrefetch = 6;    // stages whose block ids are in flight ahead of the issue
 
@@ -73,7 +73,11 @@ struct alignas(8) Job {
     int seqlen;
     int b_lo, b_hi;  // block range of the piece
     long long pre;   // KV blocks of all sequences before s
-    bool valid;
+    // Per piece, computed once when the piece starts (64-bit divisions):
+    int nsplits;     // pieces its (sequence, kv head) is cut into (1 = complete)
+    int jfirst;      // first work range holding a piece of it
+    int first_slot1; // that range stored its piece in its second slot
+    int valid;
 };
 
 template <int D, int NT, int NSTAGE>
@@ -180,11 +184,15 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         prefetch_tensormap(&tm_v);
     }
 
-    // ---- pass 1: total KV blocks; zero the outputs of empty sequences.
+    // ---- pass 1: total KV blocks. Context lengths are read from global
+    // memory once and kept in shared memory for everything that follows.
+    int* sSeqLen = reinterpret_cast<int*>(smem + L::kOffProd);
+    auto len_of = [&](int s) -> int { return s < kSeqCache ? sSeqLen[s] : p.seq_lens[s]; };
     long long my_blocks = 0;
     unsigned bad_len = 0;
     for (int s = tid; s < S; s += blockDim.x) {
         int len = p.seq_lens[s];
+        if (s < kSeqCache) sSeqLen[s] = len;
         if (len > cap_tokens) { bad_len = 1; len = cap_tokens; }
         if (len > 0) my_blocks += (len + bs - 1) / bs;
     }
@@ -200,7 +208,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
     // covers sequences j, j + grid, ... with the threads [first, first + n).
     auto zero_empty_outputs = [&](int first, int n) {
         for (int s = blockIdx.x; s < S; s += gridDim.x) {
-            if (p.seq_lens[s] <= 0) {
+            if (len_of(s) <= 0) {
                 const long long base = (long long)s * p.num_heads * D;
                 for (int e = first; e < p.num_heads * D; e += n)
                     out[base + e] = Elem<T>::from_f(0.f);
@@ -237,7 +245,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             const int s = c0 + tid;
             long long nb = 0;
             if (s < S) {
-                int len = min(p.seq_lens[s], cap_tokens);
+                int len = min(len_of(s), cap_tokens);
                 nb = len > 0 ? (len + bs - 1) / bs : 0;
             }
             long long chunk_total;
@@ -261,15 +269,6 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         return;
     }
 
-    // Context lengths of the sequences this CTA starts with, cached for the
-    // producer's walk (metadata only: allowed before griddepcontrol.wait).
-    int* sSeqLen = reinterpret_cast<int*>(smem + L::kOffProd);
-    for (int i = tid; i < kSeqCache; i += blockDim.x) {
-        const int s = s_first + i;
-        sSeqLen[i] = s < S ? p.seq_lens[s] : 0;
-    }
-    __syncthreads();
-
     if (warp == kConsumerWarps) {
         // ===================================================== producer warp
         const int bps = kStageRows / bs;  // blocks per stage
@@ -282,15 +281,14 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                                                           kJobRing * (int)sizeof(Job));
 
         auto seq_blocks = [&](int s, int& seqlen) -> int {
-            int len = s - s_first < kSeqCache ? sSeqLen[s - s_first] : p.seq_lens[s];
-            len = min(len, cap_tokens);
+            int len = min(len_of(s), cap_tokens);
             seqlen = len > 0 ? len : 0;
             return len > 0 ? (len + bs - 1) / bs : 0;
         };
         // First job of the piece that starts at unit x (x inside sequence s).
         auto piece_job = [&](long long x, int s, long long pre) -> Job {
             Job jb;
-            jb.valid = false;
+            jb.valid = 0;
             if (x >= uend || s >= S) return jb;
             int seqlen;
             int nb = seq_blocks(s, seqlen);
@@ -309,7 +307,17 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             jb.nb = nb;
             jb.seqlen = seqlen;
             jb.pre = pre;
-            jb.valid = true;
+            if (jb.b_lo == 0 && jb.b_hi == nb) {
+                jb.nsplits = 1;
+                jb.jfirst = j;
+                jb.first_slot1 = 0;
+            } else {
+                const int jf = cta_of(u_first, W, P_);
+                jb.nsplits = cta_of(u_first + nb - 1, W, P_) - jf + 1;
+                jb.jfirst = jf;
+                jb.first_slot1 = range_start(jf, W, P_) < u_first ? 1 : 0;
+            }
+            jb.valid = 1;
             return jb;
         };
         auto next_job = [&](const Job& jb) -> Job {
@@ -378,24 +386,14 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 d.nrows = job.nblk * bs;
                 d.seqlen = job.seqlen;
                 d.invalid_mask = (~vmask) & ((1u << job.nblk) - 1u);
-                const bool complete = job.b_lo == 0 && job.b_hi == job.nb;
+                const bool complete = job.nsplits == 1;
                 d.flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
                           (complete ? kPieceComplete : 0);
                 d.u = job.s * KVH + job.h;
-                if (!complete) {
-                    const long long u_first = job.pre * KVH + (long long)job.h * job.nb;
-                    const int jf = cta_of(u_first, W, P_);
-                    const int jl = cta_of(u_first + job.nb - 1, W, P_);
-                    d.nsplits = jl - jf + 1;
-                    d.jfirst = jf;
-                    d.first_slot1 = range_start(jf, W, P_) < u_first ? 1 : 0;
-                    d.slot = 2 * j + (first_piece ? 0 : 1);
-                } else {
-                    d.nsplits = 1;
-                    d.jfirst = j;
-                    d.first_slot1 = 0;
-                    d.slot = 2 * j;
-                }
+                d.nsplits = job.nsplits;
+                d.jfirst = job.jfirst;
+                d.first_slot1 = job.first_slot1;
+                d.slot = 2 * j + (first_piece ? 0 : 1);
                 const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
                                        (piece_start ? (uint32_t)(G * D * 2) : 0u);
                 mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
