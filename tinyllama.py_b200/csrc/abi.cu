@@ -141,8 +141,9 @@ WsLayout ws_layout(int64_t num_seqs, int64_t num_kv_heads, int64_t head_dim, int
     w.counters = tlb::attn::kWorkspaceHeader;
     w.ml = w.counters + align_up((size_t)num_seqs * num_kv_heads * 4, 256);
     w.zeroed = w.ml;
-    w.o = w.ml + align_up((size_t)2 * grid * gpad * 2 * 4, 256);
-    w.total = w.o + align_up((size_t)2 * grid * gpad * head_dim * 4, 256);
+    const size_t slots = (size_t)2 * tlb::attn::kItemsPerCta * grid;
+    w.o = w.ml + align_up(slots * gpad * 2 * 4, 256);
+    w.total = w.o + align_up(slots * gpad * head_dim * 4, 256);
     return w;
 }
 
@@ -255,6 +256,7 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
         p.ws_o = reinterpret_cast<float*>(ws + w.o);
         p.ws_ml = reinterpret_cast<float*>(ws + w.ml);
         p.counters = reinterpret_cast<unsigned int*>(ws + w.counters);
+        p.sched = reinterpret_cast<unsigned int*>(ws);  // header: zeroed, self-resetting
         p.num_blocks = num_blocks;
         p.num_seqs = (int)num_seqs;
         p.num_heads = (int)num_heads;

@@ -15,11 +15,14 @@ constexpr int kTileRows = 16;       // tokens per warp tile (mma k / n extent)
 constexpr int kStageRows = kConsumerWarps * kTileRows;  // tokens per pipeline stage
 constexpr int kGMax = 16;           // largest query-head group on the tensor-core path
 #ifndef TLB_ATTN_CTAS_PER_SM
-#define TLB_ATTN_CTAS_PER_SM 1
+#define TLB_ATTN_CTAS_PER_SM 2
 #endif
 // Persistent grid: at most this many CTAs per SM (also sizes the workspace).
 constexpr int kMaxCtasPerSm = TLB_ATTN_CTAS_PER_SM;
 constexpr int kWorkspaceHeader = 256;
+// Work items per CTA of the grid the partial-result slots are sized for: one
+// static range per CTA plus at most two tail chunks per CTA.
+constexpr int kItemsPerCta = 3;
 
 struct TcParams {
     void* out;
@@ -29,6 +32,7 @@ struct TcParams {
     float* ws_o;              // [2 * grid][gpad][head_dim] unnormalised partial outputs
     float* ws_ml;             // [2 * grid][gpad][2] (running max, running sum) per partial
     unsigned int* counters;   // [num_seqs * num_kv_heads] arrival counters (self-resetting)
+    unsigned int* sched;      // [2] tail-chunk counter, finished-CTA counter (self-resetting)
     long long num_blocks;
     int num_seqs;
     int num_heads;

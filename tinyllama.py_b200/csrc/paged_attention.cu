@@ -77,6 +77,8 @@ struct alignas(8) Job {
     int nsplits;     // pieces its (sequence, kv head) is cut into (1 = complete)
     int jfirst;      // first work range holding a piece of it
     int first_slot1; // that range stored its piece in its second slot
+    int item;        // work item the piece belongs to (partial slot 2*item + !first)
+    int first;       // first piece of its item
     int valid;
 };
 
@@ -99,7 +101,7 @@ struct TcLayout {
     static constexpr int kOffMisc = kOffBar + 2 * NSTAGE * 8;
     static constexpr int kMiscInts = 64;
     static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
-    static constexpr int kProdBytes = kSeqCache * 4 + kJobRing * (int)sizeof(Job) + kJobRing * 8 * 4;
+    static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * 8 * 4;
     static constexpr int kBytes = kOffProd + kProdBytes;
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
@@ -184,25 +186,41 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         prefetch_tensormap(&tm_v);
     }
 
-    // ---- pass 1: total KV blocks. Context lengths are read from global
-    // memory once and kept in shared memory for everything that follows.
+    // ---- pass 1: context lengths -> shared memory, exclusive prefix of KV
+    // blocks per sequence, total. Thread t owns sequences [t*per, t*per+per):
+    // one batch of independent loads, one block scan.
     int* sSeqLen = reinterpret_cast<int*>(smem + L::kOffProd);
+    unsigned* sPre = reinterpret_cast<unsigned*>(smem + L::kOffProd + kSeqCache * 4);
     auto len_of = [&](int s) -> int { return s < kSeqCache ? sSeqLen[s] : p.seq_lens[s]; };
-    long long my_blocks = 0;
-    unsigned bad_len = 0;
-    for (int s = tid; s < S; s += blockDim.x) {
-        int len = p.seq_lens[s];
-        if (s < kSeqCache) sSeqLen[s] = len;
-        if (len > cap_tokens) { bad_len = 1; len = cap_tokens; }
-        if (len > 0) my_blocks += (len + bs - 1) / bs;
-    }
-    if (bad_len) flag_status(TLB_STATUS_SEQ_TOO_LONG);
+    auto blocks_of = [&](int len) -> int {
+        len = min(len, cap_tokens);
+        return len > 0 ? (len + bs - 1) / bs : 0;
+    };
     long long total_blocks;
-    block_incl_scan(my_blocks, sScan, &total_blocks);
+    {
+        const int per = (S + (int)blockDim.x - 1) / (int)blockDim.x;
+        const int s0 = min(S, tid * per), s1 = min(S, s0 + per);
+        long long mine = 0;
+        unsigned bad_len = 0;
+        for (int s = s0; s < s1; ++s) {
+            const int len = p.seq_lens[s];
+            if (s < kSeqCache) sSeqLen[s] = len;
+            if (len > cap_tokens) bad_len = 1;
+            mine += blocks_of(len);
+        }
+        if (bad_len) flag_status(TLB_STATUS_SEQ_TOO_LONG);
+        long long run = block_incl_scan(mine, sScan, &total_blocks) - mine;
+        for (int s = s0; s < min(s1, kSeqCache); ++s) {
+            sPre[s] = (unsigned)run;
+            run += blocks_of(sSeqLen[s]);
+        }
+        if (tid == 0 && S < kSeqCache) sPre[S] = (unsigned)total_blocks;
+        __syncthreads();
+    }
 
     // Until griddepcontrol.wait this kernel only reads metadata (seq_lens,
-    // block_tables) and writes nothing: with programmatic launch it may be
-    // running beside the kernel before it.
+    // block_tables) and writes nothing but its own status word: with
+    // programmatic launch it may be running beside the kernel before it.
     T* out = reinterpret_cast<T*>(p.out);
     // Sequences with no context get zeros (attention_kernel.cu:102); CTA j
     // covers sequences j, j + grid, ... with the threads [first, first + n).
@@ -222,32 +240,54 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         zero_empty_outputs(tid, blockDim.x);
         return;
     }
+    // ---- work items. Items [0, P) split the first Ws units into equal
+    // contiguous ranges, one per CTA (stream-K). With the prefix cached, the
+    // last quarter of the units forms T tail chunks of C units, taken in order
+    // from an atomic counter by whichever CTA is free first, so CTAs that
+    // stream faster take more of them and all finish together.
+    const bool cached = S < kSeqCache && total_blocks < (1ll << 32);
+    const long long Ws = cached ? W - W / 4 : W;
     int P = (int)gridDim.x;
     {
-        const long long want = (W + p.min_units - 1) / p.min_units;
+        const long long want = (Ws + p.min_units - 1) / p.min_units;
         if (want < P) P = (int)(want > 0 ? want : 1);
     }
+    const long long Wt = W - Ws;
+    long long C = (Wt + 2ll * gridDim.x - 1) / (2ll * gridDim.x);
+    if (C < 4) C = 4;
+    const int T_tail = (int)((Wt + C - 1) / C);
+    auto item_start = [&](int i) -> long long {
+        return i < P ? range_start(i, Ws, P) : Ws + (long long)(i - P) * C;
+    };
+    auto item_end = [&](int i) -> long long {
+        return i < P ? range_start(i + 1, Ws, P) : min(W, Ws + (long long)(i - P + 1) * C);
+    };
+    auto item_of = [&](long long x) -> int {
+        return x < Ws ? cta_of(x, Ws, P) : P + (int)((x - Ws) / C);
+    };
     const int j = blockIdx.x;
-    if (j >= P) {
-        grid_dependency_wait();
-        zero_empty_outputs(tid, blockDim.x);
-        return;
-    }
-    const long long ustart = range_start(j, W, P);
-    const long long uend = range_start(j + 1, W, P);
 
-    // ---- pass 2: locate the sequence holding unit `ustart`.
-    if (tid == 0) sMisc[0] = -1;
-    __syncthreads();
-    {
+    // Sequence holding unit x and its block prefix: binary search of the
+    // cached prefix, or (uncached) a block-wide scan for the static item.
+    auto locate_cached = [&](long long x, long long& pre) -> int {
+        int lo = 0, hi = S - 1;  // largest s with sPre[s] * KVH <= x
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if ((long long)sPre[mid] * KVH <= x) lo = mid; else hi = mid - 1;
+        }
+        pre = sPre[lo];
+        return lo;
+    };
+    int s_first = 0;
+    long long pre_first = 0;
+    if (j < P && !cached) {
+        const long long ustart = item_start(j);
+        if (tid == 0) sMisc[0] = -1;
+        __syncthreads();
         long long base = 0;
         for (int c0 = 0; c0 < S; c0 += blockDim.x) {
             const int s = c0 + tid;
-            long long nb = 0;
-            if (s < S) {
-                int len = min(len_of(s), cap_tokens);
-                nb = len > 0 ? (len + bs - 1) / bs : 0;
-            }
+            const long long nb = s < S ? blocks_of(len_of(s)) : 0;
             long long chunk_total;
             const long long incl = block_incl_scan(nb, sScan, &chunk_total);
             const long long excl = incl - nb;
@@ -259,66 +299,78 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             base += chunk_total;
             if (base * KVH > ustart) break;
         }
-    }
-    __syncthreads();
-    const int s_first = sMisc[0];
-    const long long pre_first = reinterpret_cast<long long*>(sMisc)[1];
-    if (s_first < 0) {  // cannot happen for ustart < W; never walk from garbage
-        grid_dependency_wait();
-        zero_empty_outputs(tid, blockDim.x);
-        return;
+        __syncthreads();
+        s_first = sMisc[0];
+        pre_first = reinterpret_cast<long long*>(sMisc)[1];
+        if (s_first < 0) {  // cannot happen for ustart < W; never walk from garbage
+            grid_dependency_wait();
+            zero_empty_outputs(tid, blockDim.x);
+            return;
+        }
     }
 
     if (warp == kConsumerWarps) {
         // ===================================================== producer warp
         const int bps = kStageRows / bs;  // blocks per stage
         const uint64_t pol = l2_policy_evict_first();
-        const int P_ = P;
         const T* query = reinterpret_cast<const T*>(p.query);
-        Job* sJob = reinterpret_cast<Job*>(smem + L::kOffProd + kSeqCache * 4);
-        const uint32_t sBid = sbase + L::kOffProd + kSeqCache * 4 + kJobRing * (int)sizeof(Job);
-        const int* sBidPtr = reinterpret_cast<const int*>(smem + L::kOffProd + kSeqCache * 4 +
+        Job* sJob = reinterpret_cast<Job*>(smem + L::kOffProd + kSeqCache * 8);
+        const uint32_t sBid = sbase + L::kOffProd + kSeqCache * 8 + kJobRing * (int)sizeof(Job);
+        const int* sBidPtr = reinterpret_cast<const int*>(smem + L::kOffProd + kSeqCache * 8 +
                                                           kJobRing * (int)sizeof(Job));
 
-        auto seq_blocks = [&](int s, int& seqlen) -> int {
-            int len = min(len_of(s), cap_tokens);
-            seqlen = len > 0 ? len : 0;
-            return len > 0 ? (len + bs - 1) / bs : 0;
-        };
-        // First job of the piece that starts at unit x (x inside sequence s).
-        auto piece_job = [&](long long x, int s, long long pre) -> Job {
+        // First job of the piece that starts at unit x (inside sequence s or a
+        // later one) of work item `item`.
+        auto piece_job = [&](long long x, int s, long long pre, int item, bool first) -> Job {
             Job jb;
             jb.valid = 0;
-            if (x >= uend || s >= S) return jb;
-            int seqlen;
-            int nb = seq_blocks(s, seqlen);
+            const long long iend = item_end(item);
+            if (x >= iend || s >= S) return jb;
+            int nb = blocks_of(len_of(s));
             while (nb == 0) {  // skip empty sequences
                 if (++s >= S) return jb;
-                nb = seq_blocks(s, seqlen);
+                nb = blocks_of(len_of(s));
             }
             const long long rel = x - pre * KVH;
             jb.s = s;
             jb.h = (int)(rel / nb);
             jb.b_lo = (int)(rel % nb);
             const long long u_first = pre * KVH + (long long)jb.h * nb;
-            jb.b_hi = (int)min((long long)nb, uend - u_first);
+            jb.b_hi = (int)min((long long)nb, iend - u_first);
             jb.cb = jb.b_lo;
             jb.nblk = min(bps, jb.b_hi - jb.cb);
             jb.nb = nb;
-            jb.seqlen = seqlen;
+            jb.seqlen = max(0, min(len_of(s), cap_tokens));
             jb.pre = pre;
+            jb.item = item;
+            jb.first = first ? 1 : 0;
             if (jb.b_lo == 0 && jb.b_hi == nb) {
                 jb.nsplits = 1;
-                jb.jfirst = j;
+                jb.jfirst = item;
                 jb.first_slot1 = 0;
             } else {
-                const int jf = cta_of(u_first, W, P_);
-                jb.nsplits = cta_of(u_first + nb - 1, W, P_) - jf + 1;
+                const int jf = item_of(u_first);
+                jb.nsplits = item_of(u_first + nb - 1) - jf + 1;
                 jb.jfirst = jf;
-                jb.first_slot1 = range_start(jf, W, P_) < u_first ? 1 : 0;
+                jb.first_slot1 = item_start(jf) < u_first ? 1 : 0;
             }
             jb.valid = 1;
             return jb;
+        };
+        auto first_job_of = [&](int item) -> Job {
+            long long pre;
+            const long long x = item_start(item);
+            const int s = locate_cached(x, pre);
+            return piece_job(x, s, pre, item, true);
+        };
+        // Next tail chunk, or an invalid job when none is left.
+        auto grab = [&]() -> Job {
+            Job none;
+            none.valid = 0;
+            if (T_tail == 0) return none;
+            const int t = (int)atomicAdd(p.sched, 1u);
+            if (t >= T_tail) return none;
+            return first_job_of(P + t);
         };
         auto next_job = [&](const Job& jb) -> Job {
             if (jb.cb + jb.nblk < jb.b_hi) {
@@ -327,34 +379,55 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 n.nblk = min(bps, jb.b_hi - n.cb);
                 return n;
             }
-            // piece finished: next unit
+            // piece finished: next unit of the item, or the next item
             const long long x = jb.pre * KVH + (long long)jb.h * jb.nb + jb.b_hi;
-            if (jb.h + 1 < KVH) return piece_job(x, jb.s, jb.pre);
-            return piece_job(x, jb.s + 1, jb.pre + jb.nb);
+            if (x < item_end(jb.item)) {
+                if (jb.h + 1 < KVH) return piece_job(x, jb.s, jb.pre, jb.item, false);
+                return piece_job(x, jb.s + 1, jb.pre + jb.nb, jb.item, false);
+            }
+            return grab();
         };
 
         // Jobs are generated kPrefetch stages ahead of the one being issued:
         // the job goes to a shared ring and its block ids are copied there
         // with cp.async, so the dependent global read of the block table
-        // never sits between two TMA issues.
-        Job pj = piece_job(ustart, s_first, pre_first);
+        // never sits between two TMA issues. `pj` is the next job to store;
+        // it is advanced lazily, so nothing is taken from the tail counter
+        // before griddepcontrol.wait.
+        Job pj;
+        pj.valid = 0;
+        bool have_pj = false;
+        if (j < P) {
+            if (cached) {
+                pj = first_job_of(j);
+            } else {
+                pj = piece_job(item_start(j), s_first, pre_first, j, true);
+            }
+            have_pj = true;
+        }
         auto prefetch = [&](int k) {
+            if (!have_pj) {
+                pj = grab();
+                have_pj = true;
+            } else if (k > 0 && pj.valid) {
+                pj = next_job(pj);
+            }
             const int slot = k % kJobRing;
             if (lane == 0) sJob[slot] = pj;
             if (pj.valid && lane < pj.nblk)
                 cp_async_4(sBid + (uint32_t)(slot * 8 + lane) * 4u,
                            p.block_tables + (long long)pj.s * p.max_blocks + pj.cb + lane);
             cp_async_commit();
-            if (pj.valid) pj = next_job(pj);
         };
-        for (int k = 0; k < kPrefetch; ++k) prefetch(k);
+        if (have_pj) prefetch(0);
         // Everything above reads only metadata; the query and the cache may
         // still be written by the kernel launched just before this one.
         grid_dependency_wait();
         zero_empty_outputs(lane, 32);
+        if (!have_pj) prefetch(0);
+        for (int k = 1; k < kPrefetch; ++k) prefetch(k);
         int stage = 0;
         uint32_t phase = 0;
-        bool first_piece = true;
         bool ok = true;
         for (int k = 0;; ++k) {
             prefetch(k + kPrefetch);
@@ -393,7 +466,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 d.nsplits = job.nsplits;
                 d.jfirst = job.jfirst;
                 d.first_slot1 = job.first_slot1;
-                d.slot = 2 * j + (first_piece ? 0 : 1);
+                d.slot = 2 * job.item + (job.first ? 0 : 1);
                 const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
                                        (piece_start ? (uint32_t)(G * D * 2) : 0u);
                 mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
@@ -415,10 +488,17 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2),
                           bar_full + 8 * stage);
             }
-            if (piece_end) first_piece = false;
             if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
         }
         cp_async_wait<0>();
+        if (T_tail > 0 && lane == 0) {
+            // The last CTA to finish taking tail chunks resets the counters
+            // for the next launch (they live in the zeroed workspace prefix).
+            if (atomicAdd(p.sched + 1, 1u) == gridDim.x - 1) {
+                atomicExch(p.sched, 0u);
+                atomicExch(p.sched + 1, 0u);
+            }
+        }
         if (ok) {
             bool waited = true;
             if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
@@ -929,10 +1009,10 @@ int occupancy_t() {
 // stages (K, V and the query group) in flight, ~160 KB per SM, enough to
 // cover HBM latency under full load (bytes in flight = bandwidth x latency).
 #ifndef TLB_ATTN_STAGES_64
-#define TLB_ATTN_STAGES_64 10
+#define TLB_ATTN_STAGES_64 4
 #endif
 #ifndef TLB_ATTN_STAGES_128
-#define TLB_ATTN_STAGES_128 5
+#define TLB_ATTN_STAGES_128 2
 #endif
 constexpr int kStages64 = TLB_ATTN_STAGES_64;
 constexpr int kStages128 = TLB_ATTN_STAGES_128;
