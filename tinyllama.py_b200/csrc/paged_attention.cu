@@ -64,6 +64,12 @@ struct StageDesc {
 constexpr int kSeqCache = 2048; // context lengths kept in shared memory (first 2048 seqs)
 constexpr int kJobRing = 8;     // producer job ring (jobs generated ahead of issue)
 constexpr int kPrefetch = 6;    // stages whose block ids are in flight ahead of the issue
+#ifndef TLB_ATTN_TAIL_DEN
+#define TLB_ATTN_TAIL_DEN 4
+#endif
+// 1/kTailDen of the work is handed out as dynamically taken tail chunks
+// (0: purely static ranges).
+constexpr int kTailDen = TLB_ATTN_TAIL_DEN;
 
 // One stage job of the producer: a run of <= blocks_per_stage KV blocks of a
 // single (sequence, kv head) piece.
@@ -246,7 +252,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
     // from an atomic counter by whichever CTA is free first, so CTAs that
     // stream faster take more of them and all finish together.
     const bool cached = S < kSeqCache && total_blocks < (1ll << 32);
-    const long long Ws = cached ? W - W / 4 : W;
+    const long long Ws = (cached && kTailDen > 0) ? W - W / kTailDen : W;
     int P = (int)gridDim.x;
     {
         const long long want = (Ws + p.min_units - 1) / p.min_units;
@@ -363,14 +369,18 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             const int s = locate_cached(x, pre);
             return piece_job(x, s, pre, item, true);
         };
-        // Next tail chunk, or an invalid job when none is left.
+        // Next tail chunk, or an invalid job when none is left. Every lane of
+        // the producer warp runs the job generator in lockstep; lane 0 alone
+        // takes the chunk and broadcasts it.
         auto grab = [&]() -> Job {
             Job none;
             none.valid = 0;
             if (T_tail == 0) return none;
-            const int t = (int)atomicAdd(p.sched, 1u);
-            if (t >= T_tail) return none;
-            return first_job_of(P + t);
+            unsigned t = 0;
+            if (lane == 0) t = atomicAdd(p.sched, 1u);
+            t = __shfl_sync(0xffffffffu, t, 0);
+            if ((int)t >= T_tail) return none;
+            return first_job_of(P + (int)t);
         };
         auto next_job = [&](const Job& jb) -> Job {
             if (jb.cb + jb.nblk < jb.b_hi) {
