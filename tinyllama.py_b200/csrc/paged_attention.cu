@@ -61,11 +61,12 @@ struct StageDesc {
     int u;           // sequence * num_kv_heads + kv head
 };
 
-constexpr int kSeqCache = 2048; // context lengths kept in shared memory (first 2048 seqs)
+constexpr int kSeqCache = 1024; // context lengths kept in shared memory (first 1024 seqs)
+constexpr int kCombineCap = 512; // (split, head) pairs the shared-memory combine handles
 constexpr int kJobRing = 8;     // producer job ring (jobs generated ahead of issue)
 constexpr int kPrefetch = 6;    // stages whose block ids are in flight ahead of the issue
 #ifndef TLB_ATTN_TAIL_DEN
-#define TLB_ATTN_TAIL_DEN 4
+#define TLB_ATTN_TAIL_DEN 0
 #endif
 // 1/kTailDen of the work is handed out as dynamically taken tail chunks
 // (0: purely static ranges).
@@ -104,11 +105,14 @@ struct TcLayout {
     static constexpr int kOffL = kOffM + kConsumerWarps * kGP * 4;
     static constexpr int kOffDesc = kOffL + kConsumerWarps * kGP * 4;
     static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
-    static constexpr int kOffMisc = kOffBar + 2 * NSTAGE * 8;
+    static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 2) * 8;  // + epilogue full/empty
     static constexpr int kMiscInts = 64;
     static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
     static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * 8 * 4;
-    static constexpr int kBytes = kOffProd + kProdBytes;
+    static constexpr int kOffEpi = kOffProd + kProdBytes;             // hand-off descriptor
+    static constexpr int kOffW = kOffEpi + 64;                         // merge weights, M, L
+    static constexpr int kOffCW = kOffW + (kConsumerWarps * kGP + 2 * kGP) * 4;
+    static constexpr int kBytes = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
@@ -148,13 +152,12 @@ __device__ __forceinline__ long long range_start(int j, long long W, int P) {
 }  // namespace
 
 template <typename T, int D, int NT, int NSTAGE>
-__global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
+__global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
     paged_attention_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
     using L = TcLayout<D, NT, NSTAGE>;
     constexpr int GP = L::kGP;
     constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
-    constexpr int kConsumerThreads = kConsumerWarps * 32;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -167,6 +170,14 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
     StageDesc* sDesc = reinterpret_cast<StageDesc*>(smem + L::kOffDesc);
     const uint32_t bar_full = sbase + L::kOffBar;           // NSTAGE x 8 bytes
     const uint32_t bar_empty = bar_full + NSTAGE * 8;       // NSTAGE x 8 bytes
+    const uint32_t bar_epi_full = bar_empty + NSTAGE * 8;   // consumers -> epilogue
+    const uint32_t bar_epi_empty = bar_epi_full + 8;        // epilogue -> consumers
+    StageDesc* sEpi = reinterpret_cast<StageDesc*>(smem + L::kOffEpi);
+    float* sW = reinterpret_cast<float*>(smem + L::kOffW);
+    float* sHM = sW + kConsumerWarps * GP;
+    float* sHL = sHM + GP;
+    float* sCW = reinterpret_cast<float*>(smem + L::kOffCW);
+    float* sCL = sCW + kCombineCap;
     long long* sScan = reinterpret_cast<long long*>(smem + L::kOffMisc);  // 8 warp sums
     int* sMisc = reinterpret_cast<int*>(smem + L::kOffMisc + 8 * 8);
 
@@ -184,6 +195,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             mbar_init(bar_full + 8 * i, 1);
             mbar_init(bar_empty + 8 * i, kConsumerWarps);
         }
+        mbar_init(bar_epi_full, kConsumerWarps * 32);
+        mbar_init(bar_epi_empty, 32);
         fence_mbar_init();
         fence_proxy_async_smem();
     }
@@ -252,7 +265,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
     // from an atomic counter by whichever CTA is free first, so CTAs that
     // stream faster take more of them and all finish together.
     const bool cached = S < kSeqCache && total_blocks < (1ll << 32);
-    const long long Ws = (cached && kTailDen > 0) ? W - W / kTailDen : W;
+    const long long Ws = (cached && kTailDen > 0) ? W - W / (kTailDen > 0 ? kTailDen : 1) : W;
     int P = (int)gridDim.x;
     {
         const long long want = (Ws + p.min_units - 1) / p.min_units;
@@ -537,6 +550,147 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
         return;
     }
 
+    if (warp == kConsumerWarps + 1) {
+        // ===================================================== epilogue warp
+        // Merges the consumer warps' (m, l, O) of each finished piece, frees
+        // the hand-off buffer, then writes the output (whole piece) or an fp32
+        // partial; the last partial of a (sequence, kv head) to arrive merges
+        // all of them. None of this stalls the KV stream.
+        constexpr int kPer = GP * D / 32;  // piece elements per lane
+        uint32_t ephase = 0;
+        while (true) {
+            if (!mbar_wait_bounded(bar_epi_full, ephase)) {
+                if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
+                break;
+            }
+            const StageDesc e = *sEpi;
+            if (e.flags & kTerminate) break;
+            if (lane < G) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sM[w * GP + lane]);
+                float lt = 0.f;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) {
+                    const float wt = M == -INFINITY ? 0.f : exp2f(sM[w * GP + lane] - M);
+                    sW[w * GP + lane] = wt;
+                    lt += wt * sL[w * GP + lane];
+                }
+                sHM[lane] = M;
+                sHL[lane] = lt;
+            }
+            __syncwarp();
+            float acc[kPer];
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int el = lane + 32 * i;
+                const int h = el / D, dd = el % D;
+                float a = 0.f;
+                if (h < G) {
+#pragma unroll
+                    for (int w = 0; w < kConsumerWarps; ++w)
+                        a += sW[w * GP + h] * sO[(w * GP + h) * D + dd];
+                }
+                acc[i] = a;
+            }
+            __syncwarp();
+            mbar_arrive(bar_epi_empty);  // hand-off buffer free again
+            ephase ^= 1;
+
+            const long long out_base = ((long long)e.seq * p.num_heads + (long long)e.kvh * G) * D;
+            if (e.flags & kPieceComplete) {
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) {
+                    const int el = lane + 32 * i, h = el / D;
+                    if (h < G) {
+                        const float lt = sHL[h];
+                        out[out_base + el] = Elem<T>::from_f(lt > 0.f ? acc[i] / lt : 0.f);
+                    }
+                }
+                continue;
+            }
+            float* wo = p.ws_o + (long long)e.slot * GP * D;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int el = lane + 32 * i;
+                if (el / D < G) wo[el] = acc[i];
+            }
+            if (lane < G) {
+                p.ws_ml[((long long)e.slot * GP + lane) * 2 + 0] = sHM[lane];
+                p.ws_ml[((long long)e.slot * GP + lane) * 2 + 1] = sHL[lane];
+            }
+            // The warp barrier orders every lane's partial stores before lane
+            // 0's release-acquire increment (cumulativity); its acquire side
+            // orders the other pieces' stores before this warp's reads below.
+            __syncwarp();
+            unsigned last = 0;
+            if (lane == 0)
+                last = atomic_inc_acq_rel(p.counters + e.u, (unsigned)(e.nsplits - 1)) ==
+                       (unsigned)(e.nsplits - 1);
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+
+            // Last piece of this (sequence, kv head) to finish: merge them all.
+            const int n = e.nsplits;
+            auto slot_k = [&](int k) -> long long {
+                return 2ll * (e.jfirst + k) + ((k == 0 && e.first_slot1) ? 1 : 0);
+            };
+            if (n * GP <= kCombineCap) {
+                for (int idx = lane; idx < n * G; idx += 32) {
+                    const int k = idx / G, h = idx - (idx / G) * G;
+                    sCW[k * GP + h] = __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2 + 0);
+                    sCL[k * GP + h] = __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2 + 1);
+                }
+                __syncwarp();
+                if (lane < G) {
+                    float M = -INFINITY;
+                    for (int k = 0; k < n; ++k) M = fmaxf(M, sCW[k * GP + lane]);
+                    float lt = 0.f;
+                    for (int k = 0; k < n; ++k) {
+                        const float wt = M == -INFINITY ? 0.f : exp2f(sCW[k * GP + lane] - M);
+                        sCW[k * GP + lane] = wt;
+                        lt += wt * sCL[k * GP + lane];
+                    }
+                    sHL[lane] = lt > 0.f ? 1.f / lt : 0.f;
+                }
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
+                for (int k = 0; k < n; ++k) {
+                    const float* src = p.ws_o + slot_k(k) * GP * D;
+#pragma unroll
+                    for (int i = 0; i < kPer; ++i) {
+                        const int el = lane + 32 * i, h = el / D;
+                        if (h < G) acc[i] += sCW[k * GP + h] * __ldcg(src + el);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) {
+                    const int el = lane + 32 * i, h = el / D;
+                    if (h < G) out[out_base + el] = Elem<T>::from_f(acc[i] * sHL[h]);
+                }
+                __syncwarp();
+            } else {
+                for (int el = lane; el < G * D; el += 32) {
+                    const int h = el / D;
+                    float M = -INFINITY;
+                    for (int k = 0; k < n; ++k)
+                        M = fmaxf(M, __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2));
+                    float a = 0.f, lt = 0.f;
+                    if (M != -INFINITY) {
+                        for (int k = 0; k < n; ++k) {
+                            const float wt = exp2f(__ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2) - M);
+                            a += wt * __ldcg(p.ws_o + slot_k(k) * GP * D + el);
+                            lt += wt * __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2 + 1);
+                        }
+                    }
+                    out[out_base + el] = Elem<T>::from_f(lt > 0.f ? a / lt : 0.f);
+                }
+            }
+        }
+        return;
+    }
+
     // ======================================================== consumer warps
     const int g = lane >> 2;  // row group of the mma fragments
     const int q4 = lane & 3;  // thread in group
@@ -553,6 +707,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 
     int stage = 0;
     uint32_t phase = 0;
+    uint32_t ephase = 0;
     while (true) {
         bool got = true;
         got = mbar_wait_bounded(bar_full + 8 * stage, phase);
@@ -719,7 +874,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 
         if (!(d.flags & kPieceEnd)) continue;
 
-        // ================= piece end: merge the four warps' (m, l, O) =====
+        // ======== piece end: hand (m, l, O) of this warp to the epilogue warp
         float lsum[2];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -727,6 +882,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
             v += __shfl_xor_sync(0xffffffffu, v, 1);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
             lsum[hh] = v;
+        }
+        if (!mbar_wait_bounded(bar_epi_empty, ephase ^ 1)) {
+            if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
+            break;
         }
         if (q4 == 0) {
             sM[warp * GP + g] = m_run[0];
@@ -748,109 +907,16 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
                 base[8] = o[nt][mt][2];
                 base[D + 8] = o[nt][mt][3];
             }
-        named_bar_sync(1, kConsumerThreads);
-
-        const bool complete = (d.flags & kPieceComplete) != 0;
-        const long long out_base = ((long long)d.seq * p.num_heads + (long long)d.kvh * G) * D;
-        for (int e = tid; e < G * D; e += kConsumerThreads) {
-            const int h = e / D, dd = e - (e / D) * D;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sM[w * GP + h]);
-            float acc = 0.f, lt = 0.f;
-            if (M != -INFINITY) {
-#pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w) {
-                    const float wt = exp2f(sM[w * GP + h] - M);
-                    acc += wt * sO[(w * GP + h) * D + dd];
-                    lt += wt * sL[w * GP + h];
-                }
-            }
-            if (complete) {
-                out[out_base + e] = Elem<T>::from_f(lt > 0.f ? acc / lt : 0.f);
-            } else {
-                p.ws_o[((long long)d.slot * GP + h) * D + dd] = acc;
-                if (dd == 0) {
-                    p.ws_ml[((long long)d.slot * GP + h) * 2 + 0] = M;
-                    p.ws_ml[((long long)d.slot * GP + h) * 2 + 1] = lt;
-                }
-            }
-        }
-        if (!complete) {
-            // The barrier orders every consumer thread's partial stores before
-            // thread 0's release-acquire increment (cumulativity), and the
-            // acquire side orders the other pieces' stores before the reads
-            // of the CTA that arrives last.
-            named_bar_sync(1, kConsumerThreads);
-            if (tid == 0) {
-                const unsigned old = atomic_inc_acq_rel(p.counters + d.u, (unsigned)(d.nsplits - 1));
-                sMisc[8] = old == (unsigned)(d.nsplits - 1) ? 1 : 0;
-            }
-            named_bar_sync(1, kConsumerThreads);
-            if (sMisc[8]) {
-                // Last piece of this (sequence, kv head) to finish: merge all.
-                const int n = d.nsplits;
-                const int cap = L::kOFloats / 2;  // floats for maxima, same for sums
-                float* wM = sO;
-                float* wL = sO + cap;
-                if (n * GP <= cap) {
-                    for (int i = tid; i < n * G; i += kConsumerThreads) {
-                        const int k = i / G, h = i - (i / G) * G;
-                        const int slot = 2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
-                        wM[k * GP + h] = __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2 + 0);
-                        wL[k * GP + h] = __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2 + 1);
-                    }
-                    named_bar_sync(1, kConsumerThreads);
-                    if (tid < G) {
-                        const int h = tid;
-                        float M = -INFINITY;
-                        for (int k = 0; k < n; ++k) M = fmaxf(M, wM[k * GP + h]);
-                        float lt = 0.f;
-                        for (int k = 0; k < n; ++k) {
-                            const float wt = M == -INFINITY ? 0.f : exp2f(wM[k * GP + h] - M);
-                            wM[k * GP + h] = wt;
-                            lt += wt * wL[k * GP + h];
-                        }
-                        sL[h] = lt > 0.f ? 1.f / lt : 0.f;
-                    }
-                    named_bar_sync(1, kConsumerThreads);
-                    for (int e = tid; e < G * D; e += kConsumerThreads) {
-                        const int h = e / D, dd = e - (e / D) * D;
-                        float acc = 0.f;
-                        for (int k = 0; k < n; ++k) {
-                            const int slot =
-                                2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
-                            acc += wM[k * GP + h] *
-                                   __ldcg(p.ws_o + ((long long)slot * GP + h) * D + dd);
-                        }
-                        out[out_base + e] = Elem<T>::from_f(acc * sL[h]);
-                    }
-                } else {
-                    for (int e = tid; e < G * D; e += kConsumerThreads) {
-                        const int h = e / D, dd = e - (e / D) * D;
-                        float M = -INFINITY;
-                        for (int k = 0; k < n; ++k) {
-                            const int slot =
-                                2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
-                            M = fmaxf(M, __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2));
-                        }
-                        float acc = 0.f, lt = 0.f;
-                        if (M != -INFINITY) {
-                            for (int k = 0; k < n; ++k) {
-                                const int slot =
-                                    2 * (d.jfirst + k) + ((k == 0 && d.first_slot1) ? 1 : 0);
-                                const float wt =
-                                    exp2f(__ldcg(p.ws_ml + ((long long)slot * GP + h) * 2) - M);
-                                acc += wt * __ldcg(p.ws_o + ((long long)slot * GP + h) * D + dd);
-                                lt += wt * __ldcg(p.ws_ml + ((long long)slot * GP + h) * 2 + 1);
-                            }
-                        }
-                        out[out_base + e] = Elem<T>::from_f(lt > 0.f ? acc / lt : 0.f);
-                    }
-                }
-            }
-        }
-        named_bar_sync(1, kConsumerThreads);
+        if (tid == 0) *sEpi = d;
+        mbar_arrive(bar_epi_full);
+        ephase ^= 1;
+    }
+    // Let the epilogue warp finish once it has taken the last piece.
+    if (mbar_wait_bounded(bar_epi_empty, ephase ^ 1)) {
+        if (tid == 0) sEpi->flags = kTerminate;
+        mbar_arrive(bar_epi_full);
+    } else if (lane == 0) {
+        flag_status(TLB_STATUS_WAIT_TIMEOUT);
     }
 }
 
@@ -990,7 +1056,7 @@ cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensor
     if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3((kConsumerWarps + 1) * 32);
+    cfg.blockDim = dim3((kConsumerWarps + 2) * 32);
     cfg.dynamicSmemBytes = L::kAlloc;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1009,7 +1075,7 @@ int occupancy_t() {
         cudaSuccess)
         return 0;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kConsumerWarps + 1) * 32,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kConsumerWarps + 2) * 32,
                                                       L::kAlloc) != cudaSuccess)
         return 0;
     return n;
