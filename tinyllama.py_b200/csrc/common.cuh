@@ -66,6 +66,26 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
     }
 }
 
+// Four consecutive outputs (scaled fp32 -> storage type) with one store:
+// 8 bytes for half types, 16 for fp32.
+template <typename T> struct Vec4Out;
+template <> struct Vec4Out<__nv_bfloat16> {
+    static __device__ __forceinline__ void store(__nv_bfloat16* p, float4 v, float s) {
+        uint2 u;
+        u.x = pack2<__nv_bfloat16>(v.x * s, v.y * s);
+        u.y = pack2<__nv_bfloat16>(v.z * s, v.w * s);
+        *reinterpret_cast<uint2*>(p) = u;
+    }
+};
+template <> struct Vec4Out<__half> {
+    static __device__ __forceinline__ void store(__half* p, float4 v, float s) {
+        uint2 u;
+        u.x = pack2<__half>(v.x * s, v.y * s);
+        u.y = pack2<__half>(v.z * s, v.w * s);
+        *reinterpret_cast<uint2*>(p) = u;
+    }
+};
+
 // ------------------------------------------------------------- shared mem
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

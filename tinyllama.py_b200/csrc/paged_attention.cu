@@ -556,7 +556,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
         // the hand-off buffer, then writes the output (whole piece) or an fp32
         // partial; the last partial of a (sequence, kv head) to arrive merges
         // all of them. None of this stalls the KV stream.
-        constexpr int kPer = GP * D / 32;  // piece elements per lane
+        constexpr int kPer4 = GP * D / 128;  // float4 groups of the piece per lane
         uint32_t ephase = 0;
         while (true) {
             if (!mbar_wait_bounded(bar_epi_full, ephase)) {
@@ -580,16 +580,22 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                 sHL[lane] = lt;
             }
             __syncwarp();
-            float acc[kPer];
+            // Lane `lane` owns the float4 groups el4 = lane + 32 * i (elements
+            // 4 * el4 .. + 3 of the piece, all of one head): 16-byte shared
+            // and global accesses, independent across i.
+            float4 acc[kPer4];
 #pragma unroll
-            for (int i = 0; i < kPer; ++i) {
-                const int el = lane + 32 * i;
+            for (int i = 0; i < kPer4; ++i) {
+                const int el = 4 * (lane + 32 * i);
                 const int h = el / D, dd = el % D;
-                float a = 0.f;
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (h < G) {
 #pragma unroll
-                    for (int w = 0; w < kConsumerWarps; ++w)
-                        a += sW[w * GP + h] * sO[(w * GP + h) * D + dd];
+                    for (int w = 0; w < kConsumerWarps; ++w) {
+                        const float wt = sW[w * GP + h];
+                        const float4 v = *reinterpret_cast<const float4*>(sO + (w * GP + h) * D + dd);
+                        a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
+                    }
                 }
                 acc[i] = a;
             }
@@ -598,22 +604,26 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             ephase ^= 1;
 
             const long long out_base = ((long long)e.seq * p.num_heads + (long long)e.kvh * G) * D;
+            auto store_out = [&](int i, float scale) {
+                const int el = 4 * (lane + 32 * i);
+                Vec4Out<T>::store(out + out_base + el, acc[i], scale);
+            };
             if (e.flags & kPieceComplete) {
 #pragma unroll
-                for (int i = 0; i < kPer; ++i) {
-                    const int el = lane + 32 * i, h = el / D;
+                for (int i = 0; i < kPer4; ++i) {
+                    const int h = 4 * (lane + 32 * i) / D;
                     if (h < G) {
                         const float lt = sHL[h];
-                        out[out_base + el] = Elem<T>::from_f(lt > 0.f ? acc[i] / lt : 0.f);
+                        store_out(i, lt > 0.f ? 1.f / lt : 0.f);
                     }
                 }
                 continue;
             }
             float* wo = p.ws_o + (long long)e.slot * GP * D;
 #pragma unroll
-            for (int i = 0; i < kPer; ++i) {
-                const int el = lane + 32 * i;
-                if (el / D < G) wo[el] = acc[i];
+            for (int i = 0; i < kPer4; ++i) {
+                const int el = 4 * (lane + 32 * i);
+                if (el / D < G) *reinterpret_cast<float4*>(wo + el) = acc[i];
             }
             if (lane < G) {
                 p.ws_ml[((long long)e.slot * GP + lane) * 2 + 0] = sHM[lane];
@@ -638,8 +648,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             if (n * GP <= kCombineCap) {
                 for (int idx = lane; idx < n * G; idx += 32) {
                     const int k = idx / G, h = idx - (idx / G) * G;
-                    sCW[k * GP + h] = __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2 + 0);
-                    sCL[k * GP + h] = __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2 + 1);
+                    const float2 ml =
+                        __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot_k(k) * GP + h) * 2));
+                    sCW[k * GP + h] = ml.x;
+                    sCL[k * GP + h] = ml.y;
                 }
                 __syncwarp();
                 if (lane < G) {
@@ -655,19 +667,47 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                 }
                 __syncwarp();
 #pragma unroll
-                for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
-                for (int k = 0; k < n; ++k) {
-                    const float* src = p.ws_o + slot_k(k) * GP * D;
+                for (int i = 0; i < kPer4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                int k = 0;
+                for (; k + 1 < n; k += 2) {  // two splits' loads in flight together
+                    const float* s0 = p.ws_o + slot_k(k) * GP * D;
+                    const float* s1 = p.ws_o + slot_k(k + 1) * GP * D;
+                    float4 v0[kPer4], v1[kPer4];
 #pragma unroll
-                    for (int i = 0; i < kPer; ++i) {
-                        const int el = lane + 32 * i, h = el / D;
-                        if (h < G) acc[i] += sCW[k * GP + h] * __ldcg(src + el);
+                    for (int i = 0; i < kPer4; ++i) {
+                        const int el = 4 * (lane + 32 * i);
+                        const bool in = el / D < G;
+                        v0[i] = in ? __ldcg(reinterpret_cast<const float4*>(s0 + el)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        v1[i] = in ? __ldcg(reinterpret_cast<const float4*>(s1 + el)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int i = 0; i < kPer4; ++i) {
+                        const int h = min(4 * (lane + 32 * i) / D, GP - 1);
+                        const float w0 = sCW[k * GP + h], w1 = sCW[(k + 1) * GP + h];
+                        acc[i].x += w0 * v0[i].x + w1 * v1[i].x;
+                        acc[i].y += w0 * v0[i].y + w1 * v1[i].y;
+                        acc[i].z += w0 * v0[i].z + w1 * v1[i].z;
+                        acc[i].w += w0 * v0[i].w + w1 * v1[i].w;
+                    }
+                }
+                if (k < n) {
+                    const float* s0 = p.ws_o + slot_k(k) * GP * D;
+#pragma unroll
+                    for (int i = 0; i < kPer4; ++i) {
+                        const int el = 4 * (lane + 32 * i);
+                        const int h = el / D;
+                        if (h < G) {
+                            const float4 v = __ldcg(reinterpret_cast<const float4*>(s0 + el));
+                            const float w0 = sCW[k * GP + h];
+                            acc[i].x += w0 * v.x; acc[i].y += w0 * v.y;
+                            acc[i].z += w0 * v.z; acc[i].w += w0 * v.w;
+                        }
                     }
                 }
 #pragma unroll
-                for (int i = 0; i < kPer; ++i) {
-                    const int el = lane + 32 * i, h = el / D;
-                    if (h < G) out[out_base + el] = Elem<T>::from_f(acc[i] * sHL[h]);
+                for (int i = 0; i < kPer4; ++i) {
+                    const int h = 4 * (lane + 32 * i) / D;
+                    if (h < G) store_out(i, sHL[h]);
                 }
                 __syncwarp();
             } else {
