@@ -85,10 +85,7 @@ struct alignas(8) Job {
     int jfirst;      // first work range holding a piece of it
     int first_slot1; // that range stored its piece in its second slot
     int item;        // work item the piece belongs to (partial slot 2*item + !first)
-    int first;       // the piece starts where its item starts
-    int order;       // 0: item walked forward; 1: its last piece, 2: its first piece,
-                     // 3: the pieces in between (split pieces go first, see below)
-    long long stop;  // order 1..3: unit where the last piece starts
+    int first;       // first piece of its item
     int valid;
 };
 
@@ -379,32 +376,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             jb.valid = 1;
             return jb;
         };
-        // Start of the (sequence, kv head) holding unit x, with its sequence.
-        auto head_start = [&](long long x, int& s, long long& pre) -> long long {
-            s = locate_cached(x, pre);
-            const int nb = blocks_of(len_of(s));
-            return pre * KVH + (x - pre * KVH) / nb * nb;
-        };
-        // First job of an item. The pieces an item shares with its neighbours
-        // (at most its last and its first) are issued before the ones it owns
-        // whole, so the partial results of split sequences, and the merges of
-        // the CTA that completes them, happen early instead of at the end.
         auto first_job_of = [&](int item) -> Job {
-            const long long a = item_start(item), b = item_end(item);
-            int sa, sb;
-            long long pa, pb;
-            const long long ha = head_start(a, sa, pa);
-            const long long hb = head_start(b - 1, sb, pb);
-            if (ha == hb) {
-                Job jb = piece_job(a, sa, pa, item, true);
-                jb.order = 0;
-                jb.stop = b;
-                return jb;
-            }
-            Job jb = piece_job(hb, sb, pb, item, false);
-            jb.order = 1;
-            jb.stop = hb;
-            return jb;
+            long long pre;
+            const long long x = item_start(item);
+            const int s = locate_cached(x, pre);
+            return piece_job(x, s, pre, item, true);
         };
         // Next tail chunk, or an invalid job when none is left. Every lane of
         // the producer warp runs the job generator in lockstep; lane 0 alone
@@ -426,25 +402,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                 n.nblk = min(bps, jb.b_hi - n.cb);
                 return n;
             }
-            // piece finished: next piece of the item, or the next item
-            if (jb.order == 1) {  // its last piece is done: now its first
-                int sa;
-                long long pa;
-                const long long a = item_start(jb.item);
-                sa = locate_cached(a, pa);
-                Job n = piece_job(a, sa, pa, jb.item, true);
-                n.order = 2;
-                n.stop = jb.stop;
-                return n;
-            }
+            // piece finished: next unit of the item, or the next item
             const long long x = jb.pre * KVH + (long long)jb.h * jb.nb + jb.b_hi;
-            const long long limit = jb.order == 0 ? item_end(jb.item) : jb.stop;
-            if (x < limit) {
-                Job n = (jb.h + 1 < KVH) ? piece_job(x, jb.s, jb.pre, jb.item, false)
-                                         : piece_job(x, jb.s + 1, jb.pre + jb.nb, jb.item, false);
-                n.order = jb.order == 0 ? 0 : 3;
-                n.stop = jb.stop;
-                return n;
+            if (x < item_end(jb.item)) {
+                if (jb.h + 1 < KVH) return piece_job(x, jb.s, jb.pre, jb.item, false);
+                return piece_job(x, jb.s + 1, jb.pre + jb.nb, jb.item, false);
             }
             return grab();
         };
@@ -463,8 +425,6 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                 pj = first_job_of(j);
             } else {
                 pj = piece_job(item_start(j), s_first, pre_first, j, true);
-                pj.order = 0;
-                pj.stop = item_end(j);
             }
             have_pj = true;
         }
@@ -644,13 +604,17 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             ephase ^= 1;
 
             const long long out_base = ((long long)e.seq * p.num_heads + (long long)e.kvh * G) * D;
+            auto store_out = [&](int i, float scale) {
+                const int el = 4 * (lane + 32 * i);
+                Vec4Out<T>::store(out + out_base + el, acc[i], scale);
+            };
             if (e.flags & kPieceComplete) {
 #pragma unroll
                 for (int i = 0; i < kPer4; ++i) {
-                    const int el = 4 * (lane + 32 * i), h = el / D;
+                    const int h = 4 * (lane + 32 * i) / D;
                     if (h < G) {
                         const float lt = sHL[h];
-                        Vec4Out<T>::store(out + out_base + el, acc[i], lt > 0.f ? 1.f / lt : 0.f);
+                        store_out(i, lt > 0.f ? 1.f / lt : 0.f);
                     }
                 }
                 continue;
@@ -742,8 +706,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                 }
 #pragma unroll
                 for (int i = 0; i < kPer4; ++i) {
-                    const int el = 4 * (lane + 32 * i), h = el / D;
-                    if (h < G) Vec4Out<T>::store(out + out_base + el, acc[i], sHL[h]);
+                    const int h = 4 * (lane + 32 * i) / D;
+                    if (h < G) store_out(i, sHL[h]);
                 }
                 __syncwarp();
             } else {
