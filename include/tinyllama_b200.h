@@ -124,6 +124,33 @@ TLB_API int tlb_paged_attention(void* out, const void* query, const void* key_ca
                         size_t workspace_bytes, unsigned flags, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Paged attention with no caller-provided workspace (no counterpart in the
+ * reference, whose kernel needs no scratch).
+ *
+ * For callers that cannot allocate device memory: an engine that hands all
+ * free memory to its KV pool after profiling (as the reference's worker sizes
+ * the cache, src/worker/worker.py:31-81) has nothing left to allocate per
+ * call, and a host that binds only this header may have no CUDA allocator.
+ * Same arguments and results as tlb_paged_attention without the workspace:
+ * the scratch is a fixed __device__ array of TLB_NO_ALLOC_SCRATCH_BYTES inside
+ * the library, held by every GPU that loads it until the process exits.
+ * Batches whose scratch would not fit are rejected (TLB_ERR_WORKSPACE).
+ * The first call on a device looks the array up (cudaGetSymbolAddress) and
+ * clears it with an async memset; make that first call outside any stream
+ * capture. Calls share the array: calls whose kernels can overlap on the GPU
+ * (unordered streams) race and must not be issued. Allocates nothing.
+ * ---------------------------------------------------------------------- */
+#define TLB_NO_ALLOC_SCRATCH_BYTES (16u << 20)
+
+TLB_API int tlb_paged_attention_no_alloc(void* out, const void* query, const void* key_cache,
+                        const void* value_cache, const int32_t* block_tables,
+                        const int32_t* seq_lens, int64_t num_seqs,
+                        int64_t num_heads, int64_t num_kv_heads,
+                        int64_t head_dim, int64_t num_blocks,
+                        int64_t block_size, int64_t max_blocks_per_seq,
+                        float scale, int dtype, unsigned flags, void* stream);
+
+/* ------------------------------------------------------------------------
  * NeoX rotary embedding.
  *
  * Replaces `rotary_embedding_neox(postions, query, key, head_size,

@@ -41,6 +41,8 @@ _PROTOS = {
     "tlb_paged_attention_workspace_zeroed_bytes": [_i64, _i64, ctypes.POINTER(_sz)],
     "tlb_paged_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                             _i64, _f32, _i32, _vp, _sz, ctypes.c_uint, _vp],
+    "tlb_paged_attention_no_alloc": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                     _i64, _i64, _f32, _i32, ctypes.c_uint, _vp],
     "tlb_rotary_embedding_neox": [_vp, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64,
                                   _i64, _i64, _i64, _i64, _i32, _vp],
     "tlb_reshape_and_cache": [_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -149,6 +149,8 @@ WsLayout ws_layout(int64_t num_seqs, int64_t num_kv_heads, int64_t head_dim, int
 
 }  // namespace
 
+void tlb::set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 extern "C" {
 
 const char* tlb_last_error(void) { return g_last_error.c_str(); }

@@ -7,6 +7,9 @@
 
 namespace tlb {
 
+// Message returned by tlb_last_error() on this thread (defined in abi.cu).
+void set_last_error(const char* msg);
+
 // ------------------------------------------------------------ attention
 namespace attn {
 
