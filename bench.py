@@ -64,6 +64,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="rotating independent KV pools per GPU (profiling runs use 1)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="shape sweep (block size x batch x context x dtype x heads): one JSON "
+                         "line per point with the attention kernel's rate and the CPU oracle's")
+    ap.add_argument("--sweep-cpu-seconds", type=float, default=1.0,
+                    help="CPU oracle budget per sweep point")
     return ap.parse_args()
 
 
@@ -495,9 +500,106 @@ def run_reference(args, rank, world):
     }
 
 
+def run_sweep(args, rank, world, local):
+    """Attention over each sweep shape: 1..N GPUs, LPT-sharded batch, one line per point."""
+    import torch.distributed as dist
+
+    from cscr import attention as A
+    from paged_decode import partition as Pn
+    from paged_decode import roofline as R
+    from paged_decode import workloads as W
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    peak, peak_kind = measured_hbm_peak()
+    for spec in W.sweep_points():
+        # batch of the point per GPU (weak scaling), LPT split of the global batch
+        glob = spec.seq_lens * world
+        mine = [glob[i] for i in Pn.lpt_assign(glob, world)[rank]]
+        local_spec = W.DecodeSpec(spec.name, mine, spec.num_heads, spec.num_kv_heads,
+                                  spec.head_dim, spec.block_size, spec.dtype,
+                                  seed=spec.seed + rank)
+        layers = [W.make_batch(W.DecodeSpec(**{**local_spec.__dict__, "seed": local_spec.seed + 7 * l}),
+                               device=dev) for l in range(2)]
+        stream = torch.cuda.Stream(dev)
+
+        def attn():
+            for b in layers:
+                A.paged_attention(b.query, b.key_cache, b.value_cache, b.block_tables,
+                                  b.seq_lens, b.scale)
+
+        with torch.cuda.stream(stream):
+            attn()
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                attn()
+            for _ in range(3):
+                g.replay()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        reps = 50
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / (reps * len(layers))
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        e = 2 if spec.dtype != "float32" else 4
+        byt = R.attention_bytes(mine, spec.block_size, spec.num_heads, spec.num_kv_heads,
+                                spec.head_dim, e)
+        line = {"point": spec.name, "n_gpus": world, "tokens_per_s": round(len(glob) / (ms / 1e3), 1),
+                "us_per_launch": round(ms * 1e3, 2),
+                "hbm_gbs_per_gpu": round(byt / (ms / 1e3) / 1e9, 1),
+                "frac_of_measured_peak": round(byt / (ms / 1e3) / 1e9 / peak, 4),
+                "peak_kind": peak_kind}
+        if rank == 0 and world == 1 and args.sweep_cpu_seconds > 0:
+            line["cpu_oracle_tokens_per_s"] = sweep_cpu(layers[0], args.sweep_cpu_seconds)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        del layers, g
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def sweep_cpu(batch, seconds):
+    """Reference attention (CPU oracle, all host threads) on a bounded sample."""
+    from oracle import decode_oracle as O
+    from paged_decode import workloads as W
+
+    S = batch.num_decode
+    take = list(range(min(S, os.cpu_count() or 1)))
+    sub = W.DecodeBatch(**{**batch.__dict__})
+    sub.block_tables = batch.block_tables[take]
+    sub.seq_lens = batch.seq_lens[take]
+    kc, vc, tables, lens = W.compact_for_oracle(sub)
+    q = W.to_numpy(batch.query[take])
+    done, t0 = 0, time.perf_counter()
+    while True:
+        O.paged_attention_threads(q, kc, vc, tables, lens, batch.scale, batch.spec.dtype)
+        done += len(take)
+        if time.perf_counter() - t0 >= seconds:
+            break
+    return round(done / (time.perf_counter() - t0), 2)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.sweep:
+        run_sweep(args, rank, world, local)
+        return
     if world != args.gpus and world == 1 and args.gpus > 1:
         print(json.dumps({"error": "launch with torchrun for --gpus > 1"}))
         sys.exit(2)
