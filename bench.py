@@ -215,11 +215,14 @@ def run_ours(args, rank, world, local):
     stream = torch.cuda.Stream(dev)
 
     def step(b):
+        # Layers run back to back: each RoPE launch follows the previous
+        # layer's attention kernel, which writes none of the metadata RoPE
+        # reads before its dependency wait (as a QKV projection would not).
         q2 = b.query.view(S, H * D)
         k2 = b.key.view(S, KVH * D)
         q_rot = PE.rotary_embedding_neox_with_cache(b.positions, q2, k2, b.value, b.key_cache,
                                                     b.value_cache, b.slot_mapping, D,
-                                                    b.cos_sin_cache)
+                                                    b.cos_sin_cache, overlap_previous=True)
         return A.paged_attention(q_rot.view(S, H, D), b.key_cache, b.value_cache,
                                  b.block_tables, b.seq_lens, b.scale, overlap_prologue=True)
 

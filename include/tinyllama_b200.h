@@ -221,7 +221,16 @@ TLB_API int tlb_write_kv_cache(const void* key, const void* value, void* key_cac
  * non-null, otherwise from block_tables/positions (as tlb_write_kv_cache,
  * block_tables [num_tokens, max_blocks_per_seq] int32).
  * `value_stride` is in elements between tokens; key rows use key_stride.
+ *
+ * flags: TLB_ROPE_OVERLAP_PREVIOUS lets the launch begin while the kernel
+ * before it on `stream` finishes (programmatic dependent launch): until that
+ * kernel completes this one reads only positions, slots, block_tables and
+ * cos_sin_cache and writes nothing. Set it only when the preceding kernel
+ * does not write those four arrays (a QKV projection or an attention
+ * launch do not); leave it unset when the predecessor is unknown.
  * ---------------------------------------------------------------------- */
+#define TLB_ROPE_OVERLAP_PREVIOUS 0x1u
+
 TLB_API int tlb_rotary_embedding_neox_with_cache(
     void* out, const void* positions, int pos_dtype, const void* query,
     void* key, const void* value, void* key_cache, void* value_cache,
@@ -230,7 +239,8 @@ TLB_API int tlb_rotary_embedding_neox_with_cache(
     int64_t num_kv_heads, int64_t head_size, const void* cos_sin_cache,
     int64_t cache_rows, int64_t rot_dim, int64_t num_blocks,
     int64_t block_size, int64_t query_stride, int64_t key_stride,
-    int64_t value_stride, int64_t out_stride, int dtype, void* stream);
+    int64_t value_stride, int64_t out_stride, int dtype, unsigned flags,
+    void* stream);
 
 /* ------------------------------------------------------------------------
  * Block copies (cscr/cache.cpp:94-151, cscr/cache_kernel.cu:124-212).

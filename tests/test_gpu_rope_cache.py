@@ -143,6 +143,54 @@ def test_fused_rope_cache_equals_separate_ops(dtype, by_table, built_lib):
         assert torch.equal(x.view(torch.int16), y.view(torch.int16))
 
 
+def test_overlap_previous_waits_for_the_kernel_before_it(built_lib):
+    """With overlap_previous the fused launch starts during the attention
+    kernel before it. That attention reads the very cache rows the launch
+    writes (each sequence's newest token), so an early write would change
+    its output; the predecessor-written query must also be read fresh."""
+    from cscr import attention as A
+
+    b = W.make_batch(W.qwen3b_decode(3, batch=64))
+    S = b.num_decode
+    q_attn = b.query[:S].contiguous()
+    kc0, vc0 = b.key_cache.clone(), b.value_cache.clone()
+    ref_attn = A.paged_attention(q_attn, kc0, vc0, b.block_tables, b.seq_lens, b.scale)
+    q2 = b.query.reshape(S, -1).contiguous()
+    k0 = b.key.reshape(S, -1).clone()  # the launches rotate their key in place
+    k_ref = k0.clone()
+    kc_ref, vc_ref = kc0.clone(), vc0.clone()
+    rope_ref = PE.rotary_embedding_neox_with_cache(b.positions, q2, k_ref, b.value, kc_ref, vc_ref,
+                                                   b.slot_mapping, 128, b.cos_sin_cache)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        kc, vc = kc0.clone(), vc0.clone()
+        k = k0.clone()
+        q_in = torch.zeros_like(q2)
+        torch.cuda.synchronize()
+        q_in.copy_(q2)  # a kernel that writes the query just before the launch
+        out_attn = A.paged_attention(q_attn, kc, vc, b.block_tables, b.seq_lens, b.scale)
+        rope = PE.rotary_embedding_neox_with_cache(b.positions, q_in, k, b.value, kc, vc,
+                                                   b.slot_mapping, 128, b.cos_sin_cache,
+                                                   overlap_previous=True)
+        torch.cuda.synchronize()
+        assert torch.equal(out_attn.view(torch.int16), ref_attn.view(torch.int16))
+        for x, y in ((rope, rope_ref), (k, k_ref), (kc, kc_ref), (vc, vc_ref)):
+            assert torch.equal(x.view(torch.int16), y.view(torch.int16))
+    # after a non-kernel predecessor as well
+    kc, vc = kc0.clone(), vc0.clone()
+    k = k0.clone()
+    q_host = q2.cpu().pin_memory()
+    q_in = torch.zeros_like(q2)
+    torch.cuda.synchronize()
+    q_in.copy_(q_host, non_blocking=True)
+    rope = PE.rotary_embedding_neox_with_cache(b.positions, q_in, k, b.value, kc, vc,
+                                               b.slot_mapping, 128, b.cos_sin_cache,
+                                               overlap_previous=True)
+    torch.cuda.synchronize()
+    assert torch.equal(rope.view(torch.int16), rope_ref.view(torch.int16))
+    assert _lib.device_status() == 0
+
+
 def test_fused_rope_cache_ragged_batch_against_oracle(built_lib):
     spec = W.ragged_batch(1)
     b = W.make_batch(spec)

@@ -51,7 +51,8 @@ _PROTOS = {
                            _i64, _i64, _i32, _vp],
     "tlb_rotary_embedding_neox_with_cache": [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
                                              _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,
-                                             _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp],
+                                             _i64, _i64, _i64, _i64, _i64, _i64, _i32,
+                                             ctypes.c_uint, _vp],
     "tlb_copy_blocks": [ctypes.POINTER(_vp), _i64, ctypes.POINTER(_i64), _i64, _i64, _vp],
     "tlb_swap_blocks": [_vp, _i32, _vp, _i32, ctypes.POINTER(_i64), _i64, _i64, _vp],
     "tlb_decode_metadata": [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp],

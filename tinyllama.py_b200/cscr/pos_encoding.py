@@ -77,7 +77,8 @@ def rotary_embedding_neox_with_cache(postions: torch.Tensor, query: torch.Tensor
                                      key_cache: torch.Tensor, value_cache: torch.Tensor,
                                      slot_mapping: torch.Tensor | None, head_size: int,
                                      cos_sin_cache: torch.Tensor,
-                                     block_tables: torch.Tensor | None = None) -> torch.Tensor:
+                                     block_tables: torch.Tensor | None = None, *,
+                                     overlap_previous: bool = False) -> torch.Tensor:
     """RoPE on query/key plus the KV-cache write of the rotated key and the value.
 
     query [T, H * head_size], key [T, KVH * head_size] (rotated in place),
@@ -87,6 +88,12 @@ def rotary_embedding_neox_with_cache(postions: torch.Tensor, query: torch.Tensor
     no write) or, when slot_mapping is None, block_tables[t, pos // block_size]
     at offset pos % block_size as src/model_executor/layers/attention.py:96-116
     addresses it (negative block id = no write).
+
+    overlap_previous=True launches the kernel programmatically so that it
+    starts while the kernel before it on the stream finishes; until then it
+    reads only positions, slots, block tables and the cos/sin table. Use it
+    only when that kernel writes none of those (an attention launch or a QKV
+    projection).
     """
     out = torch.empty_like(query)
     num_tokens, rot_dim = _check_rope(postions, query, key, head_size, cos_sin_cache, out)
@@ -128,6 +135,6 @@ def rotary_embedding_neox_with_cache(postions: torch.Tensor, query: torch.Tensor
             query.size(1) // head_size, num_kv_heads, head_size, cos_sin_cache.data_ptr(),
             cos_sin_cache.size(0), rot_dim, key_cache.size(0), key_cache.size(2),
             query.stride(0), key.stride(0), v2.stride(0), out.stride(0),
-            DTYPE_CODE[query.dtype], _lib.stream_of(dev))
+            DTYPE_CODE[query.dtype], 1 if overlap_previous else 0, _lib.stream_of(dev))
         _lib.check(rc)
     return out

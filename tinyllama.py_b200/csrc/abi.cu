@@ -447,10 +447,11 @@ int tlb_rotary_embedding_neox_with_cache(
     const int32_t* block_tables, int64_t max_blocks_per_seq, int64_t num_tokens, int64_t num_heads, int64_t num_kv_heads, int64_t head_size,
     const void* cos_sin_cache, int64_t cache_rows, int64_t rot_dim, int64_t num_blocks,
     int64_t block_size, int64_t query_stride, int64_t key_stride, int64_t value_stride,
-    int64_t out_stride, int dtype, void* stream) {
+    int64_t out_stride, int dtype, unsigned flags, void* stream) {
     if (int rc = rope_checks(positions, pos_dtype, num_tokens, num_heads, num_kv_heads, head_size,
                              cos_sin_cache, cache_rows, rot_dim, dtype))
         return rc;
+    TLB_REQUIRE((flags & ~TLB_ROPE_OVERLAP_PREVIOUS) == 0, "unknown flags");
     if (int rc = cache_checks(key_cache, value_cache, num_tokens, num_kv_heads, head_size,
                               num_blocks, block_size, dtype))
         return rc;
@@ -486,6 +487,7 @@ int tlb_rotary_embedding_neox_with_cache(
     p.head_size = (int)head_size;
     p.rot_dim = (int)rot_dim;
     p.block_size = (int)block_size;
+    p.overlap = (flags & TLB_ROPE_OVERLAP_PREVIOUS) ? 1 : 0;
     const int vec =
         pick_vec(dtype, head_size, rot_dim, {query_stride, key_stride, value_stride, out_stride},
                  {out, query, key, value, key_cache, value_cache, cos_sin_cache});

@@ -103,6 +103,7 @@ struct RopeCacheParams {
     int head_size;
     int rot_dim;
     int block_size;
+    int overlap;               // launched with programmatic stream serialization
 };
 
 // Rope only (query -> out, key in place).

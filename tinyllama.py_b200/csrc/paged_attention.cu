@@ -204,6 +204,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
         prefetch_tensormap(&tm_k);
         prefetch_tensormap(&tm_v);
     }
+    // The next kernel on the stream, if launched programmatically, may start
+    // its own prologue once SMs free up; it waits for this grid to finish
+    // before it writes or reads anything this kernel produces.
+    grid_launch_dependents();
 
     // ---- pass 1: context lengths -> shared memory, exclusive prefix of KV
     // blocks per sequence, total. Thread t owns sequences [t*per, t*per+per):

@@ -49,8 +49,11 @@ struct VecIO {
             for (int i = 0; i < VEC; ++i) p[i] = Elem<T>::from_f(f[i]);
         }
     }
-    // Raw copy of VEC elements (bit-exact).
+    // Raw copy of VEC elements (bit-exact). The source is a query, key or
+    // value row, so the copy first waits for the preceding kernel when the
+    // launch was programmatic (a no-op otherwise).
     static __device__ __forceinline__ void copy(T* dst, const T* src) {
+        grid_dependency_wait();
         if constexpr (VEC * sizeof(T) == 16) {
             *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
         } else {
@@ -98,10 +101,11 @@ template <typename T, int VEC>
 __device__ __forceinline__ void rotate(const T* src, T* dst, const T* cs, int half, int i0,
                                        T* also = nullptr) {
     float x[VEC], y[VEC], c[VEC], s[VEC];
-    VecIO<T, VEC>::load(src + i0, x);
-    VecIO<T, VEC>::load(src + i0 + half, y);
     VecIO<T, VEC>::load(cs + i0, c);
     VecIO<T, VEC>::load(cs + half + i0, s);
+    grid_dependency_wait();
+    VecIO<T, VEC>::load(src + i0, x);
+    VecIO<T, VEC>::load(src + i0 + half, y);
     float xo[VEC], yo[VEC];
 #pragma unroll
     for (int k = 0; k < VEC; ++k) {
@@ -129,6 +133,12 @@ __global__ void __launch_bounds__(256) rope_cache_kernel(const RopeCacheParams p
     // attention kernel) may start its metadata prologue now; it still waits
     // for this grid to finish before reading anything written here.
     grid_launch_dependents();
+    // When this kernel itself is launched programmatically (p.overlap), it
+    // overlaps the tail of the kernel before it on the stream. Until
+    // grid_dependency_wait() it reads only positions, slot_mapping,
+    // block_tables and the cos/sin table - never query, key or value, which
+    // the kernel before it (the QKV projection in a model) produces - and it
+    // writes nothing. Without a programmatic launch the wait returns at once.
     const int half = p.rot_dim / 2;
     const int hv = half / VEC;                       // pair vectors per head
     const int pv = (p.head_size - p.rot_dim) / VEC;  // pass-through vectors per head
@@ -278,8 +288,16 @@ template <typename T, typename PI, typename SI, int VEC, bool Q, bool C, bool BT
 cudaError_t go(const RopeCacheParams& p, cudaStream_t st) {
     const long long items = items_per_token(p, VEC, Q, C) * p.num_tokens;
     if (items == 0) return cudaSuccess;
-    rope_cache_kernel<T, PI, SI, VEC, Q, C, BT><<<grid_for(items), 256, 0, st>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid_for(items));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.overlap ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, rope_cache_kernel<T, PI, SI, VEC, Q, C, BT>, p);
 }
 
 template <typename T, int VEC, bool Q, bool C, bool BT>
