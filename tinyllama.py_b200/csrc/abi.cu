@@ -92,8 +92,11 @@ struct MapKeyHash {
     }
 };
 
-// A cache viewed as a 2-D tensor [rows = blocks * kv_heads * block_size, head_dim]
-// of 16-bit elements; box = 64 columns (128 bytes, 128-byte swizzle) x block_size rows.
+// A cache [rows = blocks * kv_heads * block_size, head_dim] of 16-bit elements
+// viewed as a 3-D tensor {64 columns, rows, head_dim / 64 column chunks}
+// (strides: a row, 128 bytes). One box = one (block, kv head) tile, stored in
+// shared memory chunk-major: [chunk][block_size rows][128 bytes], 128-byte
+// swizzle, so every 8-row group of a chunk is one 1024-byte swizzle atom.
 int kv_tensor_map(const void* base, uint64_t rows, int head_dim, int box_rows, CUtensorMap* out) {
     static std::mutex mu;
     static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
@@ -108,12 +111,13 @@ int kv_tensor_map(const void* base, uint64_t rows, int head_dim, int box_rows, C
     }
     auto fn = encode_fn();
     if (fn == nullptr) return fail(TLB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
-    cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
+    const cuuint32_t chunks = (cuuint32_t)(head_dim / 64);
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, chunks};
+    cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, chunks};
+    cuuint32_t estr[3] = {1, 1, 1};
     CUtensorMap m;
-    CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+    CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides,
                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(TLB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -266,7 +270,7 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
         p.group = group;
         p.block_size = (int)block_size;
         p.max_blocks = (int)max_blocks_per_seq;
-        p.min_units = (int)(512 / block_size) > 0 ? (int)(512 / block_size) : 1;
+        p.min_units = 512 / tlb::attn::kStageRows;  // 512 tokens per CTA at least
         p.scale_log2 = scale_log2;
         e = tlb::attn::launch_tc(dtype, (int)head_dim, group, p, tk, tv, grid,
                                  (flags & TLB_ATTN_OVERLAP_PROLOGUE) != 0, st);

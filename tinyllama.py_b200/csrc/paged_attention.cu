@@ -8,9 +8,12 @@
 // negative are skipped; an empty softmax gives zeros (:102).
 //
 // Tensor-core path (fp16 / bf16, head_dim 64 or 128, group <= 16):
-//   * Work is the flat list of (sequence, kv head, KV block) units, cut into
-//     equal contiguous ranges, one per persistent CTA ("stream-K"), so every
-//     CTA streams the same number of KV bytes whatever the length mix.
+//   * Work is the flat list of (sequence, kv head, stage) units - a stage is
+//     64 tokens of one sequence, the tail stage of a sequence may be shorter -
+//     cut into equal contiguous ranges, one per persistent CTA ("stream-K"),
+//     so every CTA runs the same number of pipeline stages whatever the
+//     length mix, and a range boundary never leaves a partly filled stage
+//     inside a sequence.
 //   * Inside a CTA one producer warp walks its range and, per pipeline stage
 //     of 64 tokens, issues 2-D TMA loads (128-byte swizzle, evict-first L2
 //     policy) of each KV block straight from the paged cache, plus a bulk
@@ -76,10 +79,11 @@ constexpr int kTailDen = TLB_ATTN_TAIL_DEN;
 // single (sequence, kv head) piece.
 struct alignas(8) Job {
     int s, h, cb, nblk;
-    int nb;          // blocks of the sequence (clamped)
+    int ns;          // stages of the sequence (clamped)
     int seqlen;
     int b_lo, b_hi;  // block range of the piece
-    long long pre;   // KV blocks of all sequences before s
+    int st_hi;       // end of the piece in stages of the sequence
+    long long pre;   // stages of all sequences before s
     // Per piece, computed once when the piece starts (64-bit divisions):
     int nsplits;     // pieces its (sequence, kv head) is cut into (1 = complete)
     int jfirst;      // first work range holding a piece of it
@@ -92,7 +96,6 @@ struct alignas(8) Job {
 template <int D, int NT, int NSTAGE>
 struct TcLayout {
     static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
-    static constexpr int kChunkBytes = kStageRows * 128;
     static constexpr int kStageKV = kStageRows * D * 2;  // bytes of K (or V) per stage
     static constexpr int kQBytes = 8 * NT * D * 2;     // query group of the piece
     static constexpr int kGP = 8 * NT;                 // padded heads per piece
@@ -151,8 +154,9 @@ __device__ __forceinline__ long long range_start(int j, long long W, int P) {
 
 }  // namespace
 
+// One head tile (NT == 1) keeps two CTAs per SM: at most 168 registers.
 template <typename T, int D, int NT, int NSTAGE>
-__global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
+__global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     paged_attention_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
     using L = TcLayout<D, NT, NSTAGE>;
@@ -209,8 +213,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
     // before it writes or reads anything this kernel produces.
     grid_launch_dependents();
 
-    // ---- pass 1: context lengths -> shared memory, exclusive prefix of KV
-    // blocks per sequence, total. Thread t owns sequences [t*per, t*per+per):
+    // ---- pass 1: context lengths -> shared memory, exclusive prefix of
+    // stages per sequence, total. Thread t owns sequences [t*per, t*per+per):
     // one batch of independent loads, one block scan.
     int* sSeqLen = reinterpret_cast<int*>(smem + L::kOffProd);
     unsigned* sPre = reinterpret_cast<unsigned*>(smem + L::kOffProd + kSeqCache * 4);
@@ -219,7 +223,9 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
         len = min(len, cap_tokens);
         return len > 0 ? (len + bs - 1) / bs : 0;
     };
-    long long total_blocks;
+    const int bps = kStageRows / bs;  // KV blocks per stage
+    auto stages_of = [&](int len) -> int { return (blocks_of(len) + bps - 1) / bps; };
+    long long total_stages;
     {
         const int per = (S + (int)blockDim.x - 1) / (int)blockDim.x;
         const int s0 = min(S, tid * per), s1 = min(S, s0 + per);
@@ -229,15 +235,15 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             const int len = p.seq_lens[s];
             if (s < kSeqCache) sSeqLen[s] = len;
             if (len > cap_tokens) bad_len = 1;
-            mine += blocks_of(len);
+            mine += stages_of(len);
         }
         if (bad_len) flag_status(TLB_STATUS_SEQ_TOO_LONG);
-        long long run = block_incl_scan(mine, sScan, &total_blocks) - mine;
+        long long run = block_incl_scan(mine, sScan, &total_stages) - mine;
         for (int s = s0; s < min(s1, kSeqCache); ++s) {
             sPre[s] = (unsigned)run;
-            run += blocks_of(sSeqLen[s]);
+            run += stages_of(sSeqLen[s]);
         }
-        if (tid == 0 && S < kSeqCache) sPre[S] = (unsigned)total_blocks;
+        if (tid == 0 && S < kSeqCache) sPre[S] = (unsigned)total_stages;
         __syncthreads();
     }
 
@@ -257,7 +263,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
         }
     };
 
-    const long long W = total_blocks * KVH;
+    const long long W = total_stages * KVH;
     if (W == 0) {
         grid_dependency_wait();
         zero_empty_outputs(tid, blockDim.x);
@@ -268,7 +274,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
     // last quarter of the units forms T tail chunks of C units, taken in order
     // from an atomic counter by whichever CTA is free first, so CTAs that
     // stream faster take more of them and all finish together.
-    const bool cached = S < kSeqCache && total_blocks < (1ll << 32);
+    const bool cached = S < kSeqCache && total_stages < (1ll << 32);
     const long long Ws = (cached && kTailDen > 0) ? W - W / (kTailDen > 0 ? kTailDen : 1) : W;
     int P = (int)gridDim.x;
     {
@@ -290,7 +296,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
     };
     const int j = blockIdx.x;
 
-    // Sequence holding unit x and its block prefix: binary search of the
+    // Sequence holding unit x and its stage prefix: binary search of the
     // cached prefix, or (uncached) a block-wide scan for the static item.
     auto locate_cached = [&](long long x, long long& pre) -> int {
         int lo = 0, hi = S - 1;  // largest s with sPre[s] * KVH <= x
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
         long long base = 0;
         for (int c0 = 0; c0 < S; c0 += blockDim.x) {
             const int s = c0 + tid;
-            const long long nb = s < S ? blocks_of(len_of(s)) : 0;
+            const long long nb = s < S ? stages_of(len_of(s)) : 0;
             long long chunk_total;
             const long long incl = block_incl_scan(nb, sScan, &chunk_total);
             const long long excl = incl - nb;
@@ -334,7 +340,6 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
 
     if (warp == kConsumerWarps) {
         // ===================================================== producer warp
-        const int bps = kStageRows / bs;  // blocks per stage
         const uint64_t pol = l2_policy_evict_first();
         const T* query = reinterpret_cast<const T*>(p.query);
         Job* sJob = reinterpret_cast<Job*>(smem + L::kOffProd + kSeqCache * 8);
@@ -349,31 +354,34 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             jb.valid = 0;
             const long long iend = item_end(item);
             if (x >= iend || s >= S) return jb;
-            int nb = blocks_of(len_of(s));
-            while (nb == 0) {  // skip empty sequences
+            int ns = stages_of(len_of(s));
+            while (ns == 0) {  // skip empty sequences
                 if (++s >= S) return jb;
-                nb = blocks_of(len_of(s));
+                ns = stages_of(len_of(s));
             }
+            const int nb = blocks_of(len_of(s));
             const long long rel = x - pre * KVH;
             jb.s = s;
-            jb.h = (int)(rel / nb);
-            jb.b_lo = (int)(rel % nb);
-            const long long u_first = pre * KVH + (long long)jb.h * nb;
-            jb.b_hi = (int)min((long long)nb, iend - u_first);
+            jb.h = (int)(rel / ns);
+            const int st_lo = (int)(rel % ns);
+            const long long u_first = pre * KVH + (long long)jb.h * ns;
+            jb.st_hi = (int)min((long long)ns, iend - u_first);
+            jb.b_lo = st_lo * bps;
+            jb.b_hi = min(nb, jb.st_hi * bps);
             jb.cb = jb.b_lo;
             jb.nblk = min(bps, jb.b_hi - jb.cb);
-            jb.nb = nb;
+            jb.ns = ns;
             jb.seqlen = max(0, min(len_of(s), cap_tokens));
             jb.pre = pre;
             jb.item = item;
             jb.first = first ? 1 : 0;
-            if (jb.b_lo == 0 && jb.b_hi == nb) {
+            if (st_lo == 0 && jb.st_hi == ns) {
                 jb.nsplits = 1;
                 jb.jfirst = item;
                 jb.first_slot1 = 0;
             } else {
                 const int jf = item_of(u_first);
-                jb.nsplits = item_of(u_first + nb - 1) - jf + 1;
+                jb.nsplits = item_of(u_first + ns - 1) - jf + 1;
                 jb.jfirst = jf;
                 jb.first_slot1 = item_start(jf) < u_first ? 1 : 0;
             }
@@ -407,19 +415,22 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                 return n;
             }
             // piece finished: next unit of the item, or the next item
-            const long long x = jb.pre * KVH + (long long)jb.h * jb.nb + jb.b_hi;
+            const long long x = jb.pre * KVH + (long long)jb.h * jb.ns + jb.st_hi;
             if (x < item_end(jb.item)) {
                 if (jb.h + 1 < KVH) return piece_job(x, jb.s, jb.pre, jb.item, false);
-                return piece_job(x, jb.s + 1, jb.pre + jb.nb, jb.item, false);
+                return piece_job(x, jb.s + 1, jb.pre + jb.ns, jb.item, false);
             }
             return grab();
         };
 
-        // Jobs are generated kPrefetch stages ahead of the one being issued:
-        // the job goes to a shared ring and its block ids are copied there
-        // with cp.async, so the dependent global read of the block table
-        // never sits between two TMA issues. `pj` is the next job to store;
-        // it is advanced lazily, so nothing is taken from the tail counter
+        // Jobs are generated up to kPrefetch stages ahead of the one being
+        // issued: the job goes to a shared ring and its block ids are copied
+        // there with cp.async, so the dependent global read of the block
+        // table never sits between two TMA issues. New jobs are generated
+        // right after a stage is issued, while the producer would otherwise
+        // wait for a free stage, so the per-piece bookkeeping (64-bit
+        // divisions) never delays an issue. `pj` is the next job to store; it
+        // is advanced lazily, so nothing is taken from the tail counter
         // before griddepcontrol.wait.
         Job pj;
         pj.valid = 0;
@@ -441,24 +452,41 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             }
             const int slot = k % kJobRing;
             if (lane == 0) sJob[slot] = pj;
+            // The query group of a new piece is pulled into L2 (and its page
+            // into the TLB) kPrefetch stages before its bulk load. L2 is the
+            // coherence point, so this is safe before griddepcontrol.wait.
+            if (lane == 0 && pj.valid && pj.cb == pj.b_lo)
+                bulk_prefetch_l2(query + ((long long)pj.s * p.num_heads + (long long)pj.h * G) * D,
+                                 (uint32_t)(G * D * 2));
             if (pj.valid && lane < pj.nblk)
                 cp_async_4(sBid + (uint32_t)(slot * 8 + lane) * 4u,
                            p.block_tables + (long long)pj.s * p.max_blocks + pj.cb + lane);
             cp_async_commit();
         };
-        if (have_pj) prefetch(0);
+        int nf = 0;  // jobs generated (cp.async groups committed)
+        if (have_pj) {
+            prefetch(nf++);
+            prefetch(nf++);
+        }
         // Everything above reads only metadata; the query and the cache may
         // still be written by the kernel launched just before this one.
         grid_dependency_wait();
         zero_empty_outputs(lane, 32);
-        if (!have_pj) prefetch(0);
-        for (int k = 1; k < kPrefetch; ++k) prefetch(k);
+        while (nf < 2) prefetch(nf++);
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
         for (int k = 0;; ++k) {
-            prefetch(k + kPrefetch);
-            cp_async_wait<kPrefetch>();  // job k and its block ids have landed
+            // job k and its block ids have landed: at most nf - k - 1 of the
+            // committed groups may still be pending
+            switch (nf - k - 1) {
+                case 0: cp_async_wait<0>(); break;
+                case 1: cp_async_wait<1>(); break;
+                case 2: cp_async_wait<2>(); break;
+                case 3: cp_async_wait<3>(); break;
+                case 4: cp_async_wait<4>(); break;
+                default: cp_async_wait<5>(); break;
+            }
             __syncwarp();
             const Job job = sJob[k % kJobRing];
             if (!job.valid) break;
@@ -501,14 +529,12 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
             __syncwarp();
             if (valid) {
                 const uint32_t fb = bar_full + 8 * stage;
-                const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV + lane * bs * 128;
-                const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV + lane * bs * 128;
+                // one (block, kv head) tile per copy: [chunk][bs rows][128 B]
+                const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV + lane * bs * D * 2;
+                const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV + lane * bs * D * 2;
                 const int32_t y = (int32_t)(((long long)bid * KVH + job.h) * bs);
-#pragma unroll
-                for (int c = 0; c < L::kChunks; ++c) {
-                    tma_load_2d(kdst + c * L::kChunkBytes, &tm_k, c * 64, y, fb, pol);
-                    tma_load_2d(vdst + c * L::kChunkBytes, &tm_v, c * 64, y, fb, pol);
-                }
+                tma_load_3d(kdst, &tm_k, 0, y, 0, fb, pol);
+                tma_load_3d(vdst, &tm_v, 0, y, 0, fb, pol);
             }
             if (piece_start && lane == 0) {
                 const T* qsrc = query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
@@ -516,6 +542,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                           bar_full + 8 * stage);
             }
             if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
+            while (nf < k + 1 + kPrefetch) prefetch(nf++);
         }
         cp_async_wait<0>();
         if (T_tail > 0 && lane == 0) {
@@ -742,6 +769,12 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
     const int ld_row = (lane & 7) + ((mi >> 1) << 3);  // ldmatrix row within a 16-row tile
     const int ld_kk = (int)(mi & 1);
     const int r0 = warp * kTileRows;
+    // Stage row r lives in block tile r / bs at row r % bs; chunk c of a tile
+    // starts c * bs * 128 bytes in. Row offset of this lane's ldmatrix row:
+    const int ld_r = r0 + ld_row;
+    const uint32_t ld_off = (uint32_t)((ld_r / bs) * (bs * D * 2) + (ld_r % bs) * 128);
+    const uint32_t chunk_bytes = (uint32_t)(bs * 128);
+    const int ld_swz = ld_r & 7;  // bs is a multiple of 8: the row's place in its swizzle atom
 
     float m_run[2], l_run[2];
     float o[NT][KS][4];
@@ -803,40 +836,51 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                     const int r = idx / (L::kChunks * 8);
                     const int c = (idx / 8) % L::kChunks;
                     const int k = idx & 7;
+                    const int sr = r0 + r;
                     if (!((vmask >> r) & 1u))
-                        *reinterpret_cast<uint4*>(vrow + c * L::kChunkBytes + (r0 + r) * 128 + k * 16) =
+                        *reinterpret_cast<uint4*>(vrow + (sr / bs) * (bs * D * 2) + c * chunk_bytes +
+                                                  (sr % bs) * 128 + k * 16) =
                             make_uint4(0u, 0u, 0u, 0u);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
             }
 
-            // ---- S = Q K^T for 16 tokens (two 8-token n-tiles). Even and odd
-            // k-steps accumulate separately: two independent mma chains of
-            // half the depth, summed at the end.
-            float s_acc[2][4], s_odd[2][4];
-#pragma unroll
-            for (int n = 0; n < 2; ++n)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) s_acc[n][e] = s_odd[n][e] = 0.f;
+            // ---- S = Q K^T for 16 tokens (two 8-token n-tiles). All K
+            // fragments are loaded first; the k-steps then feed kQkChains
+            // independent accumulators per n-tile (mma.sync latency is far
+            // above its issue interval), summed at the end.
+            constexpr int kQkChains = KS < 4 ? KS : 4;
+            uint32_t kf[KS][4];
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 const int c = ks >> 2;
                 const int kk = ((ks & 3) << 1) + ld_kk;
-                const int row = r0 + ld_row;
-                const uint32_t addr =
-                    kbase + c * L::kChunkBytes + row * 128 + ((kk ^ (row & 7)) << 4);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(addr, b0, b1, b2, b3);
-                float (&acc0)[4] = (ks & 1) ? s_odd[0] : s_acc[0];
-                float (&acc1)[4] = (ks & 1) ? s_odd[1] : s_acc[1];
-                mma16816<T>(acc0, qa[ks], b0, b1);
-                mma16816<T>(acc1, qa[ks], b2, b3);
+                ldsm_x4(kbase + ld_off + c * chunk_bytes + ((kk ^ ld_swz) << 4), kf[ks][0],
+                        kf[ks][1], kf[ks][2], kf[ks][3]);
             }
+            float s_part[kQkChains][2][4];
+#pragma unroll
+            for (int ch = 0; ch < kQkChains; ++ch)
+#pragma unroll
+                for (int n = 0; n < 2; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s_part[ch][n][e] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                mma16816<T>(s_part[ks % kQkChains][0], qa[ks], kf[ks][0], kf[ks][1]);
+                mma16816<T>(s_part[ks % kQkChains][1], qa[ks], kf[ks][2], kf[ks][3]);
+            }
+            float s_acc[2][4];
 #pragma unroll
             for (int n = 0; n < 2; ++n)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) s_acc[n][e] += s_odd[n][e];
+                for (int e = 0; e < 4; ++e) {
+                    float v = s_part[0][n][e];
+#pragma unroll
+                    for (int ch = 1; ch < kQkChains; ++ch) v += s_part[ch][n][e];
+                    s_acc[n][e] = v;
+                }
 
             // ---- online softmax (log2 domain); heads g (and g + 8).
             float x[2][4];
@@ -895,21 +939,27 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32)
                 split2<T>(pr[0][2 * nt], pr[0][2 * nt + 1], pb[nt][0], pl[nt][0]);
                 split2<T>(pr[1][2 * nt], pr[1][2 * nt + 1], pb[nt][1], pl[nt][1]);
             }
-            // ---- O^T += V^T P^T, one 16-wide slice of head_dim per m-tile.
+            // ---- O^T += V^T P^T, one 16-wide slice of head_dim per m-tile:
+            // all V fragments first, then the hi products of every m-tile,
+            // then the lo products, so no mma waits on the one before it.
+            uint32_t vf[KS][4];
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
                 const int c = mt >> 2;
                 const int kk = ((mt & 3) << 1) + ld_kk;
-                const int row = r0 + ld_row;
-                const uint32_t addr =
-                    vbase + c * L::kChunkBytes + row * 128 + ((kk ^ (row & 7)) << 4);
-                uint32_t a[4];
-                ldsm_x4_trans(addr, a[0], a[1], a[2], a[3]);
+                ldsm_x4_trans(vbase + ld_off + c * chunk_bytes + ((kk ^ ld_swz) << 4), vf[mt][0],
+                              vf[mt][1], vf[mt][2], vf[mt][3]);
+            }
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    mma16816<T>(o[nt][mt], a, pb[nt][0], pb[nt][1]);
-                    if constexpr (kSplitP<T>) mma16816<T>(o[nt][mt], a, pl[nt][0], pl[nt][1]);
-                }
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) mma16816<T>(o[nt][mt], vf[mt], pb[nt][0], pb[nt][1]);
+            if constexpr (kSplitP<T>) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt)
+                        mma16816<T>(o[nt][mt], vf[mt], pl[nt][0], pl[nt][1]);
             }
         }
         __syncwarp();
