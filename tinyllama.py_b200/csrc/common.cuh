@@ -180,6 +180,15 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
         : "memory");
 }
+// One lane of the (converged, full) warp: the single-thread region that
+// issues TMA copies, so their operands are known to be warp-uniform.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
 // Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),

@@ -49,19 +49,18 @@ enum : int {
     kTerminate = 8,
 };
 
-struct StageDesc {
+// Written by the producer as three 16-byte stores.
+struct alignas(16) StageDesc {
+    unsigned rows_lo, rows_hi;  // bit r: stage row r holds a token of the piece
+    int flags;
     int seq;
     int kvh;
-    int tok0;        // token index (within the sequence) of stage row 0
-    int nrows;       // rows loaded in this stage (blocks * block_size)
-    int seqlen;      // clamped context length of the sequence
-    unsigned invalid_mask;  // bit i: block i of this stage was not loaded
-    int flags;
     int slot;        // partial slot of this piece (when not complete)
     int nsplits;     // pieces the (sequence, kv head) is cut into
     int jfirst;      // first CTA holding a piece of it
     int first_slot1; // that CTA stored its piece in its second slot
     int u;           // sequence * num_kv_heads + kv head
+    int pad0, pad1;
 };
 
 constexpr int kSeqCache = 1024; // context lengths kept in shared memory (first 1024 seqs)
@@ -106,13 +105,13 @@ struct TcLayout {
     static constexpr int kOffO = kOffQ + NSTAGE * kQBytes;
     static constexpr int kOffM = kOffO + kOFloats * 4;
     static constexpr int kOffL = kOffM + kConsumerWarps * kGP * 4;
-    static constexpr int kOffDesc = kOffL + kConsumerWarps * kGP * 4;
+    static constexpr int kOffDesc = (kOffL + kConsumerWarps * kGP * 4 + 15) / 16 * 16;
     static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
     static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 2) * 8;  // + epilogue full/empty
     static constexpr int kMiscInts = 64;
     static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
     static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * 8 * 4;
-    static constexpr int kOffEpi = kOffProd + kProdBytes;             // hand-off descriptor
+    static constexpr int kOffEpi = (kOffProd + kProdBytes + 15) / 16 * 16;  // hand-off descriptor
     static constexpr int kOffW = kOffEpi + 64;                         // merge weights, M, L
     static constexpr int kOffCW = kOffW + (kConsumerWarps * kGP + 2 * kGP) * 4;
     static constexpr int kBytes = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
@@ -506,41 +505,49 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
             const unsigned vmask = __ballot_sync(0xffffffffu, valid);
             const bool piece_start = job.cb == job.b_lo;
             const bool piece_end = job.cb + job.nblk == job.b_hi;
-            if (lane == 0) {
-                StageDesc& d = sDesc[stage];
-                d.seq = job.s;
-                d.kvh = job.h;
-                d.tok0 = job.cb * bs;
-                d.nrows = job.nblk * bs;
-                d.seqlen = job.seqlen;
-                d.invalid_mask = (~vmask) & ((1u << job.nblk) - 1u);
-                const bool complete = job.nsplits == 1;
-                d.flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
-                          (complete ? kPieceComplete : 0);
-                d.u = job.s * KVH + job.h;
-                d.nsplits = job.nsplits;
-                d.jfirst = job.jfirst;
-                d.first_slot1 = job.first_slot1;
-                d.slot = 2 * job.item + (job.first ? 0 : 1);
+            // Tile row of every block of the stage, in every lane.
+            const int32_t my_y = (int32_t)(((long long)bid * KVH + job.h) * bs);
+            int32_t ys[kStageRows / 8];
+#pragma unroll
+            for (int b = 0; b < kStageRows / 8; ++b) ys[b] = __shfl_sync(0xffffffffu, my_y, b);
+            if (elect_one()) {
+                // Valid rows: inside the stage, before the context end, in a
+                // block that is loaded.
+                const int tok0 = job.cb * bs;
+                const int nv = min(job.nblk * bs, job.seqlen - tok0);
+                unsigned long long rows = nv >= 64 ? ~0ull : (nv > 0 ? (1ull << nv) - 1ull : 0ull);
+                const unsigned long long bmask = bs >= 64 ? ~0ull : (1ull << bs) - 1ull;
+                for (unsigned inval = (~vmask) & ((1u << job.nblk) - 1u); inval != 0u;
+                     inval &= inval - 1u)
+                    rows &= ~(bmask << ((__ffs(inval) - 1) * bs));
+                const int flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
+                                  (job.nsplits == 1 ? kPieceComplete : 0);
+                int4* dw = reinterpret_cast<int4*>(&sDesc[stage]);
+                dw[0] = make_int4((int)(unsigned)rows, (int)(unsigned)(rows >> 32), flags, job.s);
+                dw[1] = make_int4(job.h, 2 * job.item + (job.first ? 0 : 1), job.nsplits,
+                                  job.jfirst);
+                dw[2] = make_int4(job.first_slot1, job.s * KVH + job.h, 0, 0);
+                const uint32_t fb = bar_full + 8 * stage;
                 const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
                                        (piece_start ? (uint32_t)(G * D * 2) : 0u);
-                mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
+                mbar_arrive_expect_tx(fb, bytes);
+                // one (block, kv head) tile per copy: [chunk][bs rows][128 B]
+                const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV;
+                const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV;
+#pragma unroll
+                for (int b = 0; b < kStageRows / 8; ++b) {
+                    if ((vmask >> b) & 1u) {
+                        tma_load_3d(kdst + b * bs * D * 2, &tm_k, 0, ys[b], 0, fb, pol);
+                        tma_load_3d(vdst + b * bs * D * 2, &tm_v, 0, ys[b], 0, fb, pol);
+                    }
+                }
+                if (piece_start) {
+                    const T* qsrc =
+                        query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
+                    bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2), fb);
+                }
             }
             __syncwarp();
-            if (valid) {
-                const uint32_t fb = bar_full + 8 * stage;
-                // one (block, kv head) tile per copy: [chunk][bs rows][128 B]
-                const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV + lane * bs * D * 2;
-                const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV + lane * bs * D * 2;
-                const int32_t y = (int32_t)(((long long)bid * KVH + job.h) * bs);
-                tma_load_3d(kdst, &tm_k, 0, y, 0, fb, pol);
-                tma_load_3d(vdst, &tm_v, 0, y, 0, fb, pol);
-            }
-            if (piece_start && lane == 0) {
-                const T* qsrc = query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
-                bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2),
-                          bar_full + 8 * stage);
-            }
             if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
             while (nf < k + 1 + kPrefetch) prefetch(nf++);
         }
@@ -817,12 +824,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         }
 
         // Valid rows of this warp's 16-token tile.
-        bool rv = false;
-        if (lane < 16) {
-            const int r = r0 + lane;
-            rv = r < d.nrows && d.tok0 + r < d.seqlen && !((d.invalid_mask >> (r / bs)) & 1u);
-        }
-        const unsigned vmask = __ballot_sync(0xffffffffu, rv) & 0xffffu;
+        const unsigned vmask = ((r0 < 32 ? d.rows_lo : d.rows_hi) >> (r0 & 31)) & 0xffffu;
 
         if (vmask != 0u) {
             const uint32_t kbase = sbase + L::kOffK + stage * L::kStageKV;
