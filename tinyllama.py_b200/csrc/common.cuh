@@ -238,6 +238,15 @@ __device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (
 
 // atomicInc with release-acquire semantics at GPU scope:
 // *p = (*p >= limit) ? 0 : *p + 1, returns the old value.
+// Acquire load / relaxed store at GPU scope.
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned atomic_inc_acq_rel(unsigned* p, unsigned limit) {
     unsigned old;
     asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"

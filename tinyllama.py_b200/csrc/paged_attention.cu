@@ -114,7 +114,8 @@ struct TcLayout {
     static constexpr int kOffEpi = (kOffProd + kProdBytes + 15) / 16 * 16;  // hand-off descriptor
     static constexpr int kOffW = kOffEpi + 64;                         // merge weights, M, L
     static constexpr int kOffCW = kOffW + (kConsumerWarps * kGP + 2 * kGP) * 4;
-    static constexpr int kBytes = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
+    static constexpr int kOffOwn = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
+    static constexpr int kBytes = kOffOwn + kGP * D * 4;  // a merging piece's own partial
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
@@ -181,6 +182,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     float* sHL = sHM + GP;
     float* sCW = reinterpret_cast<float*>(smem + L::kOffCW);
     float* sCL = sCW + kCombineCap;
+    float* sOwn = reinterpret_cast<float*>(smem + L::kOffOwn);
     long long* sScan = reinterpret_cast<long long*>(smem + L::kOffMisc);  // 8 warp sums
     int* sMisc = reinterpret_cast<int*>(smem + L::kOffMisc + 8 * 8);
 
@@ -657,89 +659,111 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 }
                 continue;
             }
-            float* wo = p.ws_o + (long long)e.slot * GP * D;
-#pragma unroll
-            for (int i = 0; i < kPer4; ++i) {
-                const int el = 4 * (lane + 32 * i);
-                if (el / D < G) *reinterpret_cast<float4*>(wo + el) = acc[i];
-            }
-            if (lane < G) {
-                p.ws_ml[((long long)e.slot * GP + lane) * 2 + 0] = sHM[lane];
-                p.ws_ml[((long long)e.slot * GP + lane) * 2 + 1] = sHL[lane];
-            }
-            // The warp barrier orders every lane's partial stores before lane
-            // 0's release-acquire increment (cumulativity); its acquire side
-            // orders the other pieces' stores before this warp's reads below.
-            __syncwarp();
-            unsigned last = 0;
-            if (lane == 0)
-                last = atomic_inc_acq_rel(p.counters + e.u, (unsigned)(e.nsplits - 1)) ==
-                       (unsigned)(e.nsplits - 1);
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) continue;
-
-            // Last piece of this (sequence, kv head) to finish: merge them all.
+            // A piece of a split (sequence, kv head). If every other piece
+            // has already published its partial (counter at nsplits - 1),
+            // this one is the last: it merges straight from registers and
+            // skips its own partial and the atomic. Otherwise it publishes
+            // and takes a ticket; the last ticket merges from the workspace.
             const int n = e.nsplits;
             auto slot_k = [&](int k) -> long long {
                 return 2ll * (e.jfirst + k) + ((k == 0 && e.first_slot1) ? 1 : 0);
             };
-            if (n * GP <= kCombineCap) {
+            const bool fits = n * GP <= kCombineCap;
+            unsigned seen = 0;
+            if (fits && lane == 0) seen = ld_acquire_gpu(p.counters + e.u);
+            seen = __shfl_sync(0xffffffffu, seen, 0);
+            bool own_in_regs = fits && seen == (unsigned)(n - 1);
+            if (own_in_regs) {
+                if (lane == 0) st_relaxed_gpu(p.counters + e.u, 0u);  // ready for the next launch
+            } else {
+                float* wo = p.ws_o + (long long)e.slot * GP * D;
+#pragma unroll
+                for (int i = 0; i < kPer4; ++i) {
+                    const int el = 4 * (lane + 32 * i);
+                    if (el / D < G) *reinterpret_cast<float4*>(wo + el) = acc[i];
+                }
+                if (lane < G) {
+                    p.ws_ml[((long long)e.slot * GP + lane) * 2 + 0] = sHM[lane];
+                    p.ws_ml[((long long)e.slot * GP + lane) * 2 + 1] = sHL[lane];
+                }
+                // The warp barrier orders every lane's partial stores before
+                // lane 0's release-acquire increment (cumulativity); its
+                // acquire side orders the other pieces' stores before this
+                // warp's reads below.
+                __syncwarp();
+                unsigned last = 0;
+                if (lane == 0)
+                    last = atomic_inc_acq_rel(p.counters + e.u, (unsigned)(n - 1)) ==
+                           (unsigned)(n - 1);
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (!last) continue;
+            }
+
+            // Last piece of this (sequence, kv head) to finish: merge them all.
+            if (fits) {
+                // A piece that was not published keeps its partial in shared
+                // memory; every piece is then read the same way and summed in
+                // the same order (pairs, ascending), whichever came last, so
+                // the result is the same bits every run.
+                int own = -1;
+                if (own_in_regs) {
+                    for (int k = 0; k < n; ++k)
+                        if (slot_k(k) == e.slot) own = k;
+#pragma unroll
+                    for (int i = 0; i < kPer4; ++i)
+                        *reinterpret_cast<float4*>(sOwn + 4 * (lane + 32 * i)) = acc[i];
+                }
                 for (int idx = lane; idx < n * G; idx += 32) {
                     const int k = idx / G, h = idx - (idx / G) * G;
-                    const float2 ml =
-                        __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot_k(k) * GP + h) * 2));
+                    float2 ml;
+                    if (k == own) {
+                        ml = make_float2(sHM[h], sHL[h]);
+                    } else {
+                        ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot_k(k) * GP + h) * 2));
+                    }
                     sCW[k * GP + h] = ml.x;
                     sCL[k * GP + h] = ml.y;
                 }
-                __syncwarp();
-                if (lane < G) {
-                    float M = -INFINITY;
-                    for (int k = 0; k < n; ++k) M = fmaxf(M, sCW[k * GP + lane]);
-                    float lt = 0.f;
-                    for (int k = 0; k < n; ++k) {
-                        const float wt = M == -INFINITY ? 0.f : exp2f(sCW[k * GP + lane] - M);
-                        sCW[k * GP + lane] = wt;
-                        lt += wt * sCL[k * GP + lane];
-                    }
-                    sHL[lane] = lt > 0.f ? 1.f / lt : 0.f;
-                }
-                __syncwarp();
+                auto load_piece = [&](int k, int i) -> float4 {
+                    const int el = 4 * (lane + 32 * i);
+                    if (el / D >= G) return make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (k == own) return *reinterpret_cast<const float4*>(sOwn + el);
+                    return __ldcg(reinterpret_cast<const float4*>(p.ws_o + slot_k(k) * GP * D + el));
+                };
 #pragma unroll
                 for (int i = 0; i < kPer4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                int k = 0;
-                for (; k + 1 < n; k += 2) {  // two splits' loads in flight together
-                    const float* s0 = p.ws_o + slot_k(k) * GP * D;
-                    const float* s1 = p.ws_o + slot_k(k + 1) * GP * D;
+                for (int k = 0; k < n; k += 2) {
+                    const bool two = k + 1 < n;
                     float4 v0[kPer4], v1[kPer4];
 #pragma unroll
                     for (int i = 0; i < kPer4; ++i) {
-                        const int el = 4 * (lane + 32 * i);
-                        const bool in = el / D < G;
-                        v0[i] = in ? __ldcg(reinterpret_cast<const float4*>(s0 + el)) : make_float4(0.f, 0.f, 0.f, 0.f);
-                        v1[i] = in ? __ldcg(reinterpret_cast<const float4*>(s1 + el)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        v0[i] = load_piece(k, i);
+                        v1[i] = two ? load_piece(k + 1, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    if (k == 0) {  // weights, while the first two pieces load
+                        __syncwarp();
+                        if (lane < G) {
+                            float M = -INFINITY;
+                            for (int kk = 0; kk < n; ++kk) M = fmaxf(M, sCW[kk * GP + lane]);
+                            float lt = 0.f;
+                            for (int kk = 0; kk < n; ++kk) {
+                                const float wt =
+                                    M == -INFINITY ? 0.f : exp2f(sCW[kk * GP + lane] - M);
+                                sCW[kk * GP + lane] = wt;
+                                lt += wt * sCL[kk * GP + lane];
+                            }
+                            sHL[lane] = lt > 0.f ? 1.f / lt : 0.f;
+                        }
+                        __syncwarp();
                     }
 #pragma unroll
                     for (int i = 0; i < kPer4; ++i) {
                         const int h = min(4 * (lane + 32 * i) / D, GP - 1);
-                        const float w0 = sCW[k * GP + h], w1 = sCW[(k + 1) * GP + h];
+                        const float w0 = sCW[k * GP + h], w1 = two ? sCW[(k + 1) * GP + h] : 0.f;
                         acc[i].x += w0 * v0[i].x + w1 * v1[i].x;
                         acc[i].y += w0 * v0[i].y + w1 * v1[i].y;
                         acc[i].z += w0 * v0[i].z + w1 * v1[i].z;
                         acc[i].w += w0 * v0[i].w + w1 * v1[i].w;
-                    }
-                }
-                if (k < n) {
-                    const float* s0 = p.ws_o + slot_k(k) * GP * D;
-#pragma unroll
-                    for (int i = 0; i < kPer4; ++i) {
-                        const int el = 4 * (lane + 32 * i);
-                        const int h = el / D;
-                        if (h < G) {
-                            const float4 v = __ldcg(reinterpret_cast<const float4*>(s0 + el));
-                            const float w0 = sCW[k * GP + h];
-                            acc[i].x += w0 * v.x; acc[i].y += w0 * v.y;
-                            acc[i].z += w0 * v.z; acc[i].w += w0 * v.w;
-                        }
                     }
                 }
 #pragma unroll
