@@ -8,12 +8,12 @@
 // negative are skipped; an empty softmax gives zeros (:102).
 //
 // Tensor-core path (fp16 / bf16, head_dim 64 or 128, group <= 16):
-//   * Work is the flat list of (sequence, kv head, stage) units - a stage is
-//     64 tokens of one sequence, the tail stage of a sequence may be shorter -
-//     cut into equal contiguous ranges, one per persistent CTA ("stream-K"),
-//     so every CTA runs the same number of pipeline stages whatever the
-//     length mix, and a range boundary never leaves a partly filled stage
-//     inside a sequence.
+//   * Work is the flat list of (sequence, kv head) units, each a run of
+//     stages of 64 tokens (the last one of a sequence may be shorter) plus a
+//     fixed charge for starting a piece, cut into equal contiguous ranges of
+//     that cost, one per persistent CTA ("stream-K"): every CTA gets the same
+//     time's worth of stages and piece starts whatever the length mix, and a
+//     range boundary never leaves a partly filled stage inside a sequence.
 //   * Inside a CTA one producer warp walks its range and, per pipeline stage
 //     of 64 tokens, issues 2-D TMA loads (128-byte swizzle, evict-first L2
 //     policy) of each KV block straight from the paged cache, plus a bulk
@@ -66,6 +66,14 @@ struct alignas(16) StageDesc {
 constexpr int kSeqCache = 1024; // context lengths kept in shared memory (first 1024 seqs)
 constexpr int kCombineCap = 512; // (split, head) pairs the shared-memory combine handles
 constexpr int kJobRing = 8;     // producer job ring (jobs generated ahead of issue)
+constexpr int kItemCache = 512; // range starts kept in shared memory (grids up to 512 CTAs)
+// Work is measured in cost units: a stage costs kCostStage, and every
+// (sequence, kv head) carries kCostPiece more for starting a piece (query
+// load, hand-off and merge), so ranges that start many pieces get fewer
+// stages. Stage i of a unit sits at cost kCostPiece + kCostStage * i from the
+// unit's start; a range owns the stages whose cost point lies inside it.
+constexpr int kCostStage = 4;
+constexpr int kCostPiece = 5;
 constexpr int kPrefetch = 6;    // stages whose block ids are in flight ahead of the issue
 #ifndef TLB_ATTN_TAIL_DEN
 #define TLB_ATTN_TAIL_DEN 0
@@ -115,7 +123,8 @@ struct TcLayout {
     static constexpr int kOffW = kOffEpi + 64;                         // merge weights, M, L
     static constexpr int kOffCW = kOffW + (kConsumerWarps * kGP + 2 * kGP) * 4;
     static constexpr int kOffOwn = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
-    static constexpr int kBytes = kOffOwn + kGP * D * 4;  // a merging piece's own partial
+    static constexpr int kOffItem = kOffOwn + kGP * D * 4;  // a merging piece's own partial
+    static constexpr int kBytes = kOffItem + (kItemCache + 1) * 8;  // start unit of each range
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
@@ -215,7 +224,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     grid_launch_dependents();
 
     // ---- pass 1: context lengths -> shared memory, exclusive prefix of
-    // stages per sequence, total. Thread t owns sequences [t*per, t*per+per):
+    // cost per sequence (per kv head), total. Thread t owns sequences [t*per, t*per+per):
     // one batch of independent loads, one block scan.
     int* sSeqLen = reinterpret_cast<int*>(smem + L::kOffProd);
     unsigned* sPre = reinterpret_cast<unsigned*>(smem + L::kOffProd + kSeqCache * 4);
@@ -226,7 +235,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     };
     const int bps = kStageRows / bs;  // KV blocks per stage
     auto stages_of = [&](int len) -> int { return (blocks_of(len) + bps - 1) / bps; };
-    long long total_stages;
+    auto cost_of = [&](int len) -> int {  // per kv head
+        const int ns = stages_of(len);
+        return ns > 0 ? kCostPiece + kCostStage * ns : 0;
+    };
+    long long total_cost;
     {
         const int per = (S + (int)blockDim.x - 1) / (int)blockDim.x;
         const int s0 = min(S, tid * per), s1 = min(S, s0 + per);
@@ -236,15 +249,15 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
             const int len = p.seq_lens[s];
             if (s < kSeqCache) sSeqLen[s] = len;
             if (len > cap_tokens) bad_len = 1;
-            mine += stages_of(len);
+            mine += cost_of(len);
         }
         if (bad_len) flag_status(TLB_STATUS_SEQ_TOO_LONG);
-        long long run = block_incl_scan(mine, sScan, &total_stages) - mine;
+        long long run = block_incl_scan(mine, sScan, &total_cost) - mine;
         for (int s = s0; s < min(s1, kSeqCache); ++s) {
             sPre[s] = (unsigned)run;
-            run += stages_of(sSeqLen[s]);
+            run += cost_of(sSeqLen[s]);
         }
-        if (tid == 0 && S < kSeqCache) sPre[S] = (unsigned)total_stages;
+        if (tid == 0 && S < kSeqCache) sPre[S] = (unsigned)total_cost;
         __syncthreads();
     }
 
@@ -264,7 +277,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         }
     };
 
-    const long long W = total_stages * KVH;
+    const long long W = total_cost * KVH;
     if (W == 0) {
         grid_dependency_wait();
         zero_empty_outputs(tid, blockDim.x);
@@ -275,29 +288,49 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     // last quarter of the units forms T tail chunks of C units, taken in order
     // from an atomic counter by whichever CTA is free first, so CTAs that
     // stream faster take more of them and all finish together.
-    const bool cached = S < kSeqCache && total_stages < (1ll << 32);
+    const bool cached = S < kSeqCache && total_cost < (1ll << 32);
     const long long Ws = (cached && kTailDen > 0) ? W - W / (kTailDen > 0 ? kTailDen : 1) : W;
     int P = (int)gridDim.x;
     {
-        const long long want = (Ws + p.min_units - 1) / p.min_units;
+        const long long min_cost = (long long)p.min_units * kCostStage;
+        const long long want = (Ws + min_cost - 1) / min_cost;
         if (want < P) P = (int)(want > 0 ? want : 1);
     }
     const long long Wt = W - Ws;
     long long C = (Wt + 2ll * gridDim.x - 1) / (2ll * gridDim.x);
     if (C < 4) C = 4;
     const int T_tail = (int)((Wt + C - 1) / C);
+    // Range starts go to shared memory once (one 64-bit division per
+    // entry, spread over the block), so the producer's per-piece lookups
+    // are loads, not divisions.
+    long long* sItem = reinterpret_cast<long long*>(smem + L::kOffItem);
+    const bool items_cached = P <= kItemCache;
+    if (items_cached) {
+        for (int i = tid; i <= P; i += blockDim.x) sItem[i] = range_start(i, Ws, P);
+    }
+    __syncthreads();
+    auto static_start = [&](int i) -> long long {
+        return items_cached ? sItem[i] : range_start(i, Ws, P);
+    };
     auto item_start = [&](int i) -> long long {
-        return i < P ? range_start(i, Ws, P) : Ws + (long long)(i - P) * C;
+        return i < P ? static_start(i) : Ws + (long long)(i - P) * C;
     };
     auto item_end = [&](int i) -> long long {
-        return i < P ? range_start(i + 1, Ws, P) : min(W, Ws + (long long)(i - P + 1) * C);
+        return i < P ? static_start(i + 1) : min(W, Ws + (long long)(i - P + 1) * C);
     };
     auto item_of = [&](long long x) -> int {
-        return x < Ws ? cta_of(x, Ws, P) : P + (int)((x - Ws) / C);
+        if (x >= Ws) return P + (int)((x - Ws) / C);
+        if (!items_cached) return cta_of(x, Ws, P);
+        // float estimate of floor(x P / Ws), corrected against the table
+        int g = (int)((float)x * ((float)P / (float)Ws));
+        g = max(0, min(P - 1, g));
+        while (g > 0 && sItem[g] > x) --g;
+        while (g + 1 < P && sItem[g + 1] <= x) ++g;
+        return g;
     };
     const int j = blockIdx.x;
 
-    // Sequence holding unit x and its stage prefix: binary search of the
+    // Sequence holding cost point x and its cost prefix: binary search of the
     // cached prefix, or (uncached) a block-wide scan for the static item.
     auto locate_cached = [&](long long x, long long& pre) -> int {
         int lo = 0, hi = S - 1;  // largest s with sPre[s] * KVH <= x
@@ -317,7 +350,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         long long base = 0;
         for (int c0 = 0; c0 < S; c0 += blockDim.x) {
             const int s = c0 + tid;
-            const long long nb = s < S ? stages_of(len_of(s)) : 0;
+            const long long nb = s < S ? cost_of(len_of(s)) : 0;
             long long chunk_total;
             const long long incl = block_incl_scan(nb, sScan, &chunk_total);
             const long long excl = incl - nb;
@@ -348,46 +381,78 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         const int* sBidPtr = reinterpret_cast<const int*>(smem + L::kOffProd + kSeqCache * 8 +
                                                           kJobRing * (int)sizeof(Job));
 
-        // First job of the piece that starts at unit x (inside sequence s or a
-        // later one) of work item `item`.
+        // First job of the first piece at or after cost point x (inside
+        // sequence s, whose cost prefix is `pre`, or a later one) of work
+        // item `item`; invalid when the item holds no further stage.
         auto piece_job = [&](long long x, int s, long long pre, int item, bool first) -> Job {
             Job jb;
             jb.valid = 0;
             const long long iend = item_end(item);
-            if (x >= iend || s >= S) return jb;
-            int ns = stages_of(len_of(s));
-            while (ns == 0) {  // skip empty sequences
-                if (++s >= S) return jb;
-                ns = stages_of(len_of(s));
+            while (true) {
+                if (x >= iend || s >= S) return jb;
+                const int len = len_of(s);
+                const int ns = stages_of(len);
+                if (ns == 0) {  // empty sequence: no cost, nothing to do
+                    ++s;
+                    continue;
+                }
+                const int L1 = kCostPiece + kCostStage * ns;  // cost of one unit
+                const long long rel = x - pre * KVH;          // < KVH * L1
+                int h, r;
+                if (rel < 0x7fffffffll) {
+                    h = (int)((unsigned)rel / (unsigned)L1);
+                    r = (int)((unsigned)rel - (unsigned)h * (unsigned)L1);
+                } else {
+                    h = (int)(rel / L1);
+                    r = (int)(rel % L1);
+                }
+                const long long U = pre * KVH + (long long)h * L1;  // unit start
+                // first stage whose cost point is at or after x
+                const int i_lo = r <= kCostPiece ? 0 : (r - kCostPiece + kCostStage - 1) / kCostStage;
+                if (i_lo >= ns) {  // past this unit's last stage: next unit
+                    x = U + L1;
+                    if (h + 1 >= KVH) {
+                        pre += L1;
+                        ++s;
+                    }
+                    continue;
+                }
+                const long long end_r = iend - U;
+                const int i_hi =
+                    end_r <= kCostPiece
+                        ? 0
+                        : (int)min((long long)ns,
+                                   (end_r - kCostPiece + kCostStage - 1) / kCostStage);
+                if (i_hi <= i_lo) return jb;  // the range ends before the next stage
+                const int nb = blocks_of(len);
+                jb.s = s;
+                jb.h = h;
+                jb.st_hi = i_hi;
+                jb.b_lo = i_lo * bps;
+                jb.b_hi = min(nb, i_hi * bps);
+                jb.cb = jb.b_lo;
+                jb.nblk = min(bps, jb.b_hi - jb.cb);
+                jb.ns = ns;
+                jb.seqlen = max(0, min(len, cap_tokens));
+                jb.pre = pre;
+                jb.item = item;
+                jb.first = first ? 1 : 0;
+                if (i_lo == 0 && i_hi == ns) {
+                    jb.nsplits = 1;
+                    jb.jfirst = item;
+                    jb.first_slot1 = 0;
+                } else {
+                    // owners of the first and the last stage; the first owner
+                    // holds an earlier stage (the previous unit's last, at
+                    // U - kCostStage) when its range starts at or before it
+                    const int jf = item_of(U + kCostPiece);
+                    jb.nsplits = item_of(U + kCostPiece + (long long)kCostStage * (ns - 1)) - jf + 1;
+                    jb.jfirst = jf;
+                    jb.first_slot1 = (U > 0 && item_start(jf) <= U - kCostStage) ? 1 : 0;
+                }
+                jb.valid = 1;
+                return jb;
             }
-            const int nb = blocks_of(len_of(s));
-            const long long rel = x - pre * KVH;
-            jb.s = s;
-            jb.h = (int)(rel / ns);
-            const int st_lo = (int)(rel % ns);
-            const long long u_first = pre * KVH + (long long)jb.h * ns;
-            jb.st_hi = (int)min((long long)ns, iend - u_first);
-            jb.b_lo = st_lo * bps;
-            jb.b_hi = min(nb, jb.st_hi * bps);
-            jb.cb = jb.b_lo;
-            jb.nblk = min(bps, jb.b_hi - jb.cb);
-            jb.ns = ns;
-            jb.seqlen = max(0, min(len_of(s), cap_tokens));
-            jb.pre = pre;
-            jb.item = item;
-            jb.first = first ? 1 : 0;
-            if (st_lo == 0 && jb.st_hi == ns) {
-                jb.nsplits = 1;
-                jb.jfirst = item;
-                jb.first_slot1 = 0;
-            } else {
-                const int jf = item_of(u_first);
-                jb.nsplits = item_of(u_first + ns - 1) - jf + 1;
-                jb.jfirst = jf;
-                jb.first_slot1 = item_start(jf) < u_first ? 1 : 0;
-            }
-            jb.valid = 1;
-            return jb;
         };
         auto first_job_of = [&](int item) -> Job {
             long long pre;
@@ -415,11 +480,15 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 n.nblk = min(bps, jb.b_hi - n.cb);
                 return n;
             }
-            // piece finished: next unit of the item, or the next item
-            const long long x = jb.pre * KVH + (long long)jb.h * jb.ns + jb.st_hi;
-            if (x < item_end(jb.item)) {
-                if (jb.h + 1 < KVH) return piece_job(x, jb.s, jb.pre, jb.item, false);
-                return piece_job(x, jb.s + 1, jb.pre + jb.ns, jb.item, false);
+            // piece finished: the next unit of the item when the piece ran to
+            // its unit's end, else (or if nothing is left) the next item
+            if (jb.st_hi == jb.ns) {
+                const long long x = jb.pre * KVH + (long long)(jb.h + 1) * (kCostPiece + kCostStage * jb.ns);
+                const Job n = jb.h + 1 < KVH
+                                  ? piece_job(x, jb.s, jb.pre, jb.item, false)
+                                  : piece_job(x, jb.s + 1, jb.pre + kCostPiece + kCostStage * jb.ns,
+                                              jb.item, false);
+                if (n.valid) return n;
             }
             return grab();
         };
