@@ -125,6 +125,14 @@ struct TcLayout {
     static constexpr int kOffOwn = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
     static constexpr int kOffItem = kOffOwn + kGP * D * 4;  // a merging piece's own partial
     static constexpr int kBytes = kOffItem + (kItemCache + 1) * 8;  // start unit of each range
+    // TMA destinations sit on 1024-byte swizzle atoms; float4 / 16-byte
+    // structures on 16 bytes.
+    static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kStageKV % 1024 == 0, "TMA tiles");
+    static_assert(kOffQ % 16 == 0 && kQBytes % 16 == 0, "bulk copy of the query");
+    static_assert(kOffO % 16 == 0 && kOffDesc % 16 == 0 && kOffEpi % 16 == 0 && kOffW % 16 == 0,
+                  "16-byte accesses");
+    static_assert(kOffOwn % 16 == 0 && kOffBar % 8 == 0 && kOffItem % 8 == 0 && kOffProd % 8 == 0,
+                  "aligned words");
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
