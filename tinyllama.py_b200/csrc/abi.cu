@@ -216,6 +216,7 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
                         void* workspace, size_t workspace_bytes, unsigned flags,
                         void* stream) {
     TLB_REQUIRE(is_float(dtype), "dtype must be float16, bfloat16 or float32");
+    TLB_REQUIRE((flags & ~TLB_ATTN_OVERLAP_PROLOGUE) == 0, "unknown flags");
     TLB_REQUIRE(num_seqs > 0, "query must contain at least one sequence");
     TLB_REQUIRE(num_heads > 0 && num_kv_heads > 0 && head_dim > 0 && num_blocks > 0 &&
                     block_size > 0 && max_blocks_per_seq > 0,

@@ -74,7 +74,14 @@ constexpr int kItemCache = 512; // range starts kept in shared memory (grids up 
 // unit's start; a range owns the stages whose cost point lies inside it.
 constexpr int kCostStage = 4;
 constexpr int kCostPiece = 5;
-constexpr int kPrefetch = 6;    // stages whose block ids are in flight ahead of the issue
+#ifndef TLB_ATTN_PREFETCH
+#define TLB_ATTN_PREFETCH 3
+#endif
+// Stage jobs generated (block ids in flight) ahead of the one being issued;
+// at most two jobs are generated per issued stage, so the lookahead never
+// comes as a burst between two issues.
+constexpr int kPrefetch = TLB_ATTN_PREFETCH;
+static_assert(kPrefetch >= 1 && kPrefetch <= 6, "cp.async group waits handle up to 5 pending");
 #ifndef TLB_ATTN_TAIL_DEN
 #define TLB_ATTN_TAIL_DEN 0
 #endif
@@ -541,7 +548,75 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                            p.block_tables + (long long)pj.s * p.max_blocks + pj.cb + lane);
             cp_async_commit();
         };
+        // Waits until job k and its block ids have landed: at most
+        // nf - k - 1 of the committed cp.async groups may still be pending.
+        auto wait_job = [&](int nf_, int k) {
+            switch (nf_ - k - 1) {
+                case 0: cp_async_wait<0>(); break;
+                case 1: cp_async_wait<1>(); break;
+                case 2: cp_async_wait<2>(); break;
+                case 3: cp_async_wait<3>(); break;
+                case 4: cp_async_wait<4>(); break;
+                default: cp_async_wait<5>(); break;
+            }
+            __syncwarp();
+        };
+        // Loaded blocks of stage job k (bit b: block b of the stage) and the
+        // tile row of every block, in every lane.
+        auto stage_blocks = [&](const Job& job, int k, int32_t (&ys)[kStageRows / 8]) -> unsigned {
+            const int bid = lane < job.nblk ? sBidPtr[(k % kJobRing) * 8 + lane] : -1;
+            const bool in_range = lane < job.nblk;
+            const bool valid = in_range && bid >= 0 && (long long)bid < p.num_blocks;
+            if (in_range && (long long)bid >= p.num_blocks) flag_status(TLB_STATUS_BAD_BLOCK_ID);
+            const int32_t my_y = (int32_t)(((long long)bid * KVH + job.h) * bs);
+#pragma unroll
+            for (int b = 0; b < kStageRows / 8; ++b) ys[b] = __shfl_sync(0xffffffffu, my_y, b);
+            return __ballot_sync(0xffffffffu, valid);
+        };
+        // Descriptor and transaction count of a stage (elected lane).
+        auto arm_stage = [&](const Job& job, int stage, unsigned vmask) {
+            const bool piece_start = job.cb == job.b_lo;
+            const bool piece_end = job.cb + job.nblk == job.b_hi;
+            // Valid rows: inside the stage, before the context end, in a
+            // block that is loaded.
+            const int tok0 = job.cb * bs;
+            const int nv = min(job.nblk * bs, job.seqlen - tok0);
+            unsigned long long rows = nv >= 64 ? ~0ull : (nv > 0 ? (1ull << nv) - 1ull : 0ull);
+            const unsigned long long bmask = bs >= 64 ? ~0ull : (1ull << bs) - 1ull;
+            for (unsigned inval = (~vmask) & ((1u << job.nblk) - 1u); inval != 0u; inval &= inval - 1u)
+                rows &= ~(bmask << ((__ffs(inval) - 1) * bs));
+            const int flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
+                              (job.nsplits == 1 ? kPieceComplete : 0);
+            int4* dw = reinterpret_cast<int4*>(&sDesc[stage]);
+            dw[0] = make_int4((int)(unsigned)rows, (int)(unsigned)(rows >> 32), flags, job.s);
+            dw[1] = make_int4(job.h, 2 * job.item + (job.first ? 0 : 1), job.nsplits, job.jfirst);
+            dw[2] = make_int4(job.first_slot1, job.s * KVH + job.h, 0, 0);
+            const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
+                                   (piece_start ? (uint32_t)(G * D * 2) : 0u);
+            mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
+        };
+        // The copies of the blocks in `mask` (one (block, kv head) tile per
+        // copy: [chunk][bs rows][128 B]) and, if asked, of the query group.
+        auto issue_copies = [&](const Job& job, int stage, unsigned mask,
+                                const int32_t (&ys)[kStageRows / 8], bool with_query) {
+            const uint32_t fb = bar_full + 8 * stage;
+            const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV;
+            const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV;
+#pragma unroll
+            for (int b = 0; b < kStageRows / 8; ++b) {
+                if ((mask >> b) & 1u) {
+                    tma_load_3d(kdst + b * bs * D * 2, &tm_k, 0, ys[b], 0, fb, pol);
+                    tma_load_3d(vdst + b * bs * D * 2, &tm_v, 0, ys[b], 0, fb, pol);
+                }
+            }
+            if (with_query) {
+                const T* qsrc = query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
+                bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2), fb);
+            }
+        };
         int nf = 0;  // jobs generated (cp.async groups committed)
+        int stage = 0;
+        uint32_t phase = 0;
         if (have_pj) {
             prefetch(nf++);
             prefetch(nf++);
@@ -551,24 +626,12 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         grid_dependency_wait();
         zero_empty_outputs(lane, 32);
         while (nf < 2) prefetch(nf++);
-        int stage = 0;
-        uint32_t phase = 0;
         bool ok = true;
         for (int k = 0;; ++k) {
-            // job k and its block ids have landed: at most nf - k - 1 of the
-            // committed groups may still be pending
-            switch (nf - k - 1) {
-                case 0: cp_async_wait<0>(); break;
-                case 1: cp_async_wait<1>(); break;
-                case 2: cp_async_wait<2>(); break;
-                case 3: cp_async_wait<3>(); break;
-                case 4: cp_async_wait<4>(); break;
-                default: cp_async_wait<5>(); break;
-            }
-            __syncwarp();
+            if (k >= nf) break;  // never read a ring slot no job was written to
+            wait_job(nf, k);
             const Job job = sJob[k % kJobRing];
             if (!job.valid) break;
-            const int bid = lane < job.nblk ? sBidPtr[(k % kJobRing) * 8 + lane] : -1;
 
             bool waited = true;
             if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
@@ -578,57 +641,15 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 ok = false;
                 break;
             }
-            const bool in_range = lane < job.nblk;
-            const bool valid = in_range && bid >= 0 && (long long)bid < p.num_blocks;
-            if (in_range && (long long)bid >= p.num_blocks) flag_status(TLB_STATUS_BAD_BLOCK_ID);
-            const unsigned vmask = __ballot_sync(0xffffffffu, valid);
-            const bool piece_start = job.cb == job.b_lo;
-            const bool piece_end = job.cb + job.nblk == job.b_hi;
-            // Tile row of every block of the stage, in every lane.
-            const int32_t my_y = (int32_t)(((long long)bid * KVH + job.h) * bs);
             int32_t ys[kStageRows / 8];
-#pragma unroll
-            for (int b = 0; b < kStageRows / 8; ++b) ys[b] = __shfl_sync(0xffffffffu, my_y, b);
+            const unsigned vmask = stage_blocks(job, k, ys);
             if (elect_one()) {
-                // Valid rows: inside the stage, before the context end, in a
-                // block that is loaded.
-                const int tok0 = job.cb * bs;
-                const int nv = min(job.nblk * bs, job.seqlen - tok0);
-                unsigned long long rows = nv >= 64 ? ~0ull : (nv > 0 ? (1ull << nv) - 1ull : 0ull);
-                const unsigned long long bmask = bs >= 64 ? ~0ull : (1ull << bs) - 1ull;
-                for (unsigned inval = (~vmask) & ((1u << job.nblk) - 1u); inval != 0u;
-                     inval &= inval - 1u)
-                    rows &= ~(bmask << ((__ffs(inval) - 1) * bs));
-                const int flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
-                                  (job.nsplits == 1 ? kPieceComplete : 0);
-                int4* dw = reinterpret_cast<int4*>(&sDesc[stage]);
-                dw[0] = make_int4((int)(unsigned)rows, (int)(unsigned)(rows >> 32), flags, job.s);
-                dw[1] = make_int4(job.h, 2 * job.item + (job.first ? 0 : 1), job.nsplits,
-                                  job.jfirst);
-                dw[2] = make_int4(job.first_slot1, job.s * KVH + job.h, 0, 0);
-                const uint32_t fb = bar_full + 8 * stage;
-                const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
-                                       (piece_start ? (uint32_t)(G * D * 2) : 0u);
-                mbar_arrive_expect_tx(fb, bytes);
-                // one (block, kv head) tile per copy: [chunk][bs rows][128 B]
-                const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV;
-                const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV;
-#pragma unroll
-                for (int b = 0; b < kStageRows / 8; ++b) {
-                    if ((vmask >> b) & 1u) {
-                        tma_load_3d(kdst + b * bs * D * 2, &tm_k, 0, ys[b], 0, fb, pol);
-                        tma_load_3d(vdst + b * bs * D * 2, &tm_v, 0, ys[b], 0, fb, pol);
-                    }
-                }
-                if (piece_start) {
-                    const T* qsrc =
-                        query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
-                    bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2), fb);
-                }
+                arm_stage(job, stage, vmask);
+                issue_copies(job, stage, vmask, ys, job.cb == job.b_lo);
             }
             __syncwarp();
             if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
-            while (nf < k + 1 + kPrefetch) prefetch(nf++);
+            for (int t = 0; t < 2 && nf < k + 1 + kPrefetch; ++t) prefetch(nf++);
         }
         cp_async_wait<0>();
         if (T_tail > 0 && lane == 0) {
