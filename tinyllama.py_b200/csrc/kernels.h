@@ -43,7 +43,7 @@ struct TcParams {
     int group;                // num_heads / num_kv_heads
     int block_size;
     int max_blocks;
-    int min_units;            // fewest stages a CTA is given before more CTAs join
+    int min_tokens;           // fewest tokens (per kv head) a CTA is given before more join
     float scale_log2;         // softmax scale * log2(e)
 };
 

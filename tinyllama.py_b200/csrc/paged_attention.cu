@@ -51,7 +51,7 @@ enum : int {
 
 // Written by the producer as three 16-byte stores.
 struct alignas(16) StageDesc {
-    unsigned rows_lo, rows_hi;  // bit r: stage row r holds a token of the piece
+    unsigned rows[4];  // bit r of word r / 32: stage row r holds a token of the piece
     int flags;
     int seq;
     int kvh;
@@ -60,7 +60,6 @@ struct alignas(16) StageDesc {
     int jfirst;      // first CTA holding a piece of it
     int first_slot1; // that CTA stored its piece in its second slot
     int u;           // sequence * num_kv_heads + kv head
-    int pad0, pad1;
 };
 
 constexpr int kSeqCache = 1024; // context lengths kept in shared memory (first 1024 seqs)
@@ -107,28 +106,29 @@ struct alignas(8) Job {
     int valid;
 };
 
-template <int D, int NT, int NSTAGE>
+template <int D, int NT, int NSTAGE, int CW>
 struct TcLayout {
+    static constexpr int kRows = CW * kTileRows;      // tokens per stage
     static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
-    static constexpr int kStageKV = kStageRows * D * 2;  // bytes of K (or V) per stage
+    static constexpr int kStageKV = kRows * D * 2;  // bytes of K (or V) per stage
     static constexpr int kQBytes = 8 * NT * D * 2;     // query group of the piece
     static constexpr int kGP = 8 * NT;                 // padded heads per piece
-    static constexpr int kOFloats = kConsumerWarps * kGP * D;
+    static constexpr int kOFloats = CW * kGP * D;
     static constexpr int kOffK = 0;
     static constexpr int kOffV = kOffK + NSTAGE * kStageKV;
     static constexpr int kOffQ = kOffV + NSTAGE * kStageKV;
     static constexpr int kOffO = kOffQ + NSTAGE * kQBytes;
     static constexpr int kOffM = kOffO + kOFloats * 4;
-    static constexpr int kOffL = kOffM + kConsumerWarps * kGP * 4;
-    static constexpr int kOffDesc = (kOffL + kConsumerWarps * kGP * 4 + 15) / 16 * 16;
+    static constexpr int kOffL = kOffM + CW * kGP * 4;
+    static constexpr int kOffDesc = (kOffL + CW * kGP * 4 + 15) / 16 * 16;
     static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
     static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 2) * 8;  // + epilogue full/empty
     static constexpr int kMiscInts = 64;
     static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
-    static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * 8 * 4;
+    static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * (kRows / 8) * 4;
     static constexpr int kOffEpi = (kOffProd + kProdBytes + 15) / 16 * 16;  // hand-off descriptor
     static constexpr int kOffW = kOffEpi + 64;                         // merge weights, M, L
-    static constexpr int kOffCW = kOffW + (kConsumerWarps * kGP + 2 * kGP) * 4;
+    static constexpr int kOffCW = kOffW + (CW * kGP + 2 * kGP) * 4;
     static constexpr int kOffOwn = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
     static constexpr int kOffItem = kOffOwn + kGP * D * 4;  // a merging piece's own partial
     static constexpr int kBytes = kOffItem + (kItemCache + 1) * 8;  // start unit of each range
@@ -179,11 +179,14 @@ __device__ __forceinline__ long long range_start(int j, long long W, int P) {
 }  // namespace
 
 // One head tile (NT == 1) keeps two CTAs per SM: at most 168 registers.
-template <typename T, int D, int NT, int NSTAGE>
-__global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
+template <typename T, int D, int NT, int NSTAGE, int CW>
+__global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     paged_attention_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
-    using L = TcLayout<D, NT, NSTAGE>;
+    using L = TcLayout<D, NT, NSTAGE, CW>;
+    constexpr int ROWS = L::kRows;        // tokens per stage
+    constexpr int kBpsMax = ROWS / 8;     // most KV blocks in a stage (block_size >= 8)
+    constexpr int kCS = kCostStage * ROWS / 64;  // cost of one stage of ROWS tokens
     constexpr int GP = L::kGP;
     constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
 
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     const uint32_t bar_epi_empty = bar_epi_full + 8;        // epilogue -> consumers
     StageDesc* sEpi = reinterpret_cast<StageDesc*>(smem + L::kOffEpi);
     float* sW = reinterpret_cast<float*>(smem + L::kOffW);
-    float* sHM = sW + kConsumerWarps * GP;
+    float* sHM = sW + CW * GP;
     float* sHL = sHM + GP;
     float* sCW = reinterpret_cast<float*>(smem + L::kOffCW);
     float* sCL = sCW + kCombineCap;
@@ -222,14 +225,14 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; ++i) {
             mbar_init(bar_full + 8 * i, 1);
-            mbar_init(bar_empty + 8 * i, kConsumerWarps);
+            mbar_init(bar_empty + 8 * i, CW);
         }
-        mbar_init(bar_epi_full, kConsumerWarps * 32);
+        mbar_init(bar_epi_full, CW * 32);
         mbar_init(bar_epi_empty, 32);
         fence_mbar_init();
         fence_proxy_async_smem();
     }
-    if (warp == kConsumerWarps && lane == 0) {
+    if (warp == CW && lane == 0) {
         prefetch_tensormap(&tm_k);
         prefetch_tensormap(&tm_v);
     }
@@ -248,11 +251,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         len = min(len, cap_tokens);
         return len > 0 ? (len + bs - 1) / bs : 0;
     };
-    const int bps = kStageRows / bs;  // KV blocks per stage
+    const int bps = ROWS / bs;  // KV blocks per stage
     auto stages_of = [&](int len) -> int { return (blocks_of(len) + bps - 1) / bps; };
     auto cost_of = [&](int len) -> int {  // per kv head
         const int ns = stages_of(len);
-        return ns > 0 ? kCostPiece + kCostStage * ns : 0;
+        return ns > 0 ? kCostPiece + kCS * ns : 0;
     };
     long long total_cost;
     {
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
     const long long Ws = (cached && kTailDen > 0) ? W - W / (kTailDen > 0 ? kTailDen : 1) : W;
     int P = (int)gridDim.x;
     {
-        const long long min_cost = (long long)p.min_units * kCostStage;
+        const long long min_cost = (long long)max(1, p.min_tokens / ROWS) * kCS;
         const long long want = (Ws + min_cost - 1) / min_cost;
         if (want < P) P = (int)(want > 0 ? want : 1);
     }
@@ -387,7 +390,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         }
     }
 
-    if (warp == kConsumerWarps) {
+    if (warp == CW) {
         // ===================================================== producer warp
         const uint64_t pol = l2_policy_evict_first();
         const T* query = reinterpret_cast<const T*>(p.query);
@@ -411,7 +414,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                     ++s;
                     continue;
                 }
-                const int L1 = kCostPiece + kCostStage * ns;  // cost of one unit
+                const int L1 = kCostPiece + kCS * ns;  // cost of one unit
                 const long long rel = x - pre * KVH;          // < KVH * L1
                 int h, r;
                 if (rel < 0x7fffffffll) {
@@ -423,7 +426,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 }
                 const long long U = pre * KVH + (long long)h * L1;  // unit start
                 // first stage whose cost point is at or after x
-                const int i_lo = r <= kCostPiece ? 0 : (r - kCostPiece + kCostStage - 1) / kCostStage;
+                const int i_lo = r <= kCostPiece ? 0 : (r - kCostPiece + kCS - 1) / kCS;
                 if (i_lo >= ns) {  // past this unit's last stage: next unit
                     x = U + L1;
                     if (h + 1 >= KVH) {
@@ -437,7 +440,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                     end_r <= kCostPiece
                         ? 0
                         : (int)min((long long)ns,
-                                   (end_r - kCostPiece + kCostStage - 1) / kCostStage);
+                                   (end_r - kCostPiece + kCS - 1) / kCS);
                 if (i_hi <= i_lo) return jb;  // the range ends before the next stage
                 const int nb = blocks_of(len);
                 jb.s = s;
@@ -459,11 +462,11 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 } else {
                     // owners of the first and the last stage; the first owner
                     // holds an earlier stage (the previous unit's last, at
-                    // U - kCostStage) when its range starts at or before it
+                    // U - kCS) when its range starts at or before it
                     const int jf = item_of(U + kCostPiece);
-                    jb.nsplits = item_of(U + kCostPiece + (long long)kCostStage * (ns - 1)) - jf + 1;
+                    jb.nsplits = item_of(U + kCostPiece + (long long)kCS * (ns - 1)) - jf + 1;
                     jb.jfirst = jf;
-                    jb.first_slot1 = (U > 0 && item_start(jf) <= U - kCostStage) ? 1 : 0;
+                    jb.first_slot1 = (U > 0 && item_start(jf) <= U - kCS) ? 1 : 0;
                 }
                 jb.valid = 1;
                 return jb;
@@ -498,10 +501,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
             // piece finished: the next unit of the item when the piece ran to
             // its unit's end, else (or if nothing is left) the next item
             if (jb.st_hi == jb.ns) {
-                const long long x = jb.pre * KVH + (long long)(jb.h + 1) * (kCostPiece + kCostStage * jb.ns);
+                const long long x = jb.pre * KVH + (long long)(jb.h + 1) * (kCostPiece + kCS * jb.ns);
                 const Job n = jb.h + 1 < KVH
                                   ? piece_job(x, jb.s, jb.pre, jb.item, false)
-                                  : piece_job(x, jb.s + 1, jb.pre + kCostPiece + kCostStage * jb.ns,
+                                  : piece_job(x, jb.s + 1, jb.pre + kCostPiece + kCS * jb.ns,
                                               jb.item, false);
                 if (n.valid) return n;
             }
@@ -544,7 +547,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 bulk_prefetch_l2(query + ((long long)pj.s * p.num_heads + (long long)pj.h * G) * D,
                                  (uint32_t)(G * D * 2));
             if (pj.valid && lane < pj.nblk)
-                cp_async_4(sBid + (uint32_t)(slot * 8 + lane) * 4u,
+                cp_async_4(sBid + (uint32_t)(slot * kBpsMax + lane) * 4u,
                            p.block_tables + (long long)pj.s * p.max_blocks + pj.cb + lane);
             cp_async_commit();
         };
@@ -563,14 +566,14 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         };
         // Loaded blocks of stage job k (bit b: block b of the stage) and the
         // tile row of every block, in every lane.
-        auto stage_blocks = [&](const Job& job, int k, int32_t (&ys)[kStageRows / 8]) -> unsigned {
-            const int bid = lane < job.nblk ? sBidPtr[(k % kJobRing) * 8 + lane] : -1;
+        auto stage_blocks = [&](const Job& job, int k, int32_t (&ys)[kBpsMax]) -> unsigned {
+            const int bid = lane < job.nblk ? sBidPtr[(k % kJobRing) * kBpsMax + lane] : -1;
             const bool in_range = lane < job.nblk;
             const bool valid = in_range && bid >= 0 && (long long)bid < p.num_blocks;
             if (in_range && (long long)bid >= p.num_blocks) flag_status(TLB_STATUS_BAD_BLOCK_ID);
             const int32_t my_y = (int32_t)(((long long)bid * KVH + job.h) * bs);
 #pragma unroll
-            for (int b = 0; b < kStageRows / 8; ++b) ys[b] = __shfl_sync(0xffffffffu, my_y, b);
+            for (int b = 0; b < kBpsMax; ++b) ys[b] = __shfl_sync(0xffffffffu, my_y, b);
             return __ballot_sync(0xffffffffu, valid);
         };
         // Descriptor and transaction count of a stage (elected lane).
@@ -581,16 +584,26 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
             // block that is loaded.
             const int tok0 = job.cb * bs;
             const int nv = min(job.nblk * bs, job.seqlen - tok0);
-            unsigned long long rows = nv >= 64 ? ~0ull : (nv > 0 ? (1ull << nv) - 1ull : 0ull);
-            const unsigned long long bmask = bs >= 64 ? ~0ull : (1ull << bs) - 1ull;
-            for (unsigned inval = (~vmask) & ((1u << job.nblk) - 1u); inval != 0u; inval &= inval - 1u)
-                rows &= ~(bmask << ((__ffs(inval) - 1) * bs));
+            unsigned rows[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const int lo = 32 * w;
+                rows[w] = nv >= lo + 32 ? ~0u : (nv > lo ? (1u << (nv - lo)) - 1u : 0u);
+            }
+            for (unsigned inval = (~vmask) & ((1u << job.nblk) - 1u); inval != 0u; inval &= inval - 1u) {
+                const int r0b = (__ffs(inval) - 1) * bs;  // rows [r0b, r0b + bs) of a missing block
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const int a = max(r0b, 32 * w) - 32 * w, b = min(r0b + bs, 32 * w + 32) - 32 * w;
+                    if (a < b) rows[w] &= ~((b - a >= 32 ? ~0u : ((1u << (b - a)) - 1u)) << a);
+                }
+            }
             const int flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
                               (job.nsplits == 1 ? kPieceComplete : 0);
             int4* dw = reinterpret_cast<int4*>(&sDesc[stage]);
-            dw[0] = make_int4((int)(unsigned)rows, (int)(unsigned)(rows >> 32), flags, job.s);
-            dw[1] = make_int4(job.h, 2 * job.item + (job.first ? 0 : 1), job.nsplits, job.jfirst);
-            dw[2] = make_int4(job.first_slot1, job.s * KVH + job.h, 0, 0);
+            dw[0] = make_int4((int)rows[0], (int)rows[1], (int)rows[2], (int)rows[3]);
+            dw[1] = make_int4(flags, job.s, job.h, 2 * job.item + (job.first ? 0 : 1));
+            dw[2] = make_int4(job.nsplits, job.jfirst, job.first_slot1, job.s * KVH + job.h);
             const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
                                    (piece_start ? (uint32_t)(G * D * 2) : 0u);
             mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
@@ -598,12 +611,12 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         // The copies of the blocks in `mask` (one (block, kv head) tile per
         // copy: [chunk][bs rows][128 B]) and, if asked, of the query group.
         auto issue_copies = [&](const Job& job, int stage, unsigned mask,
-                                const int32_t (&ys)[kStageRows / 8], bool with_query) {
+                                const int32_t (&ys)[kBpsMax], bool with_query) {
             const uint32_t fb = bar_full + 8 * stage;
             const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV;
             const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV;
 #pragma unroll
-            for (int b = 0; b < kStageRows / 8; ++b) {
+            for (int b = 0; b < kBpsMax; ++b) {
                 if ((mask >> b) & 1u) {
                     tma_load_3d(kdst + b * bs * D * 2, &tm_k, 0, ys[b], 0, fb, pol);
                     tma_load_3d(vdst + b * bs * D * 2, &tm_v, 0, ys[b], 0, fb, pol);
@@ -641,7 +654,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 ok = false;
                 break;
             }
-            int32_t ys[kStageRows / 8];
+            int32_t ys[kBpsMax];
             const unsigned vmask = stage_blocks(job, k, ys);
             if (elect_one()) {
                 arm_stage(job, stage, vmask);
@@ -688,7 +701,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         return;
     }
 
-    if (warp == kConsumerWarps + 1) {
+    if (warp == CW + 1) {
         // ===================================================== epilogue warp
         // Merges the consumer warps' (m, l, O) of each finished piece, frees
         // the hand-off buffer, then writes the output (whole piece) or an fp32
@@ -706,10 +719,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
             if (lane < G) {
                 float M = -INFINITY;
 #pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sM[w * GP + lane]);
+                for (int w = 0; w < CW; ++w) M = fmaxf(M, sM[w * GP + lane]);
                 float lt = 0.f;
 #pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w) {
+                for (int w = 0; w < CW; ++w) {
                     const float wt = M == -INFINITY ? 0.f : exp2f(sM[w * GP + lane] - M);
                     sW[w * GP + lane] = wt;
                     lt += wt * sL[w * GP + lane];
@@ -729,7 +742,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
                 float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (h < G) {
 #pragma unroll
-                    for (int w = 0; w < kConsumerWarps; ++w) {
+                    for (int w = 0; w < CW; ++w) {
                         const float wt = sW[w * GP + h];
                         const float4 v = *reinterpret_cast<const float4*>(sO + (w * GP + h) * D + dd);
                         a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
@@ -946,7 +959,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 2) * 32, NT == 1 ? 2 : 1)
         }
 
         // Valid rows of this warp's 16-token tile.
-        const unsigned vmask = ((r0 < 32 ? d.rows_lo : d.rows_hi) >> (r0 & 31)) & 0xffffu;
+        const unsigned vmask = (sDesc[stage].rows[r0 >> 5] >> (r0 & 31)) & 0xffffu;
 
         if (vmask != 0u) {
             const uint32_t kbase = sbase + L::kOffK + stage * L::kStageKV;
@@ -1257,11 +1270,11 @@ __global__ void __launch_bounds__(256) paged_attention_generic_kernel(const Gene
 // ============================================================ host side
 namespace {
 
-template <typename T, int D, int NT, int NSTAGE>
+template <typename T, int D, int NT, int NSTAGE, int CW>
 cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensorMap& tv,
                         int grid, bool overlap, cudaStream_t st) {
-    using L = TcLayout<D, NT, NSTAGE>;
-    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE>;
+    using L = TcLayout<D, NT, NSTAGE, CW>;
+    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE, CW>;
     static std::once_flag once[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1274,7 +1287,7 @@ cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensor
     if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3((kConsumerWarps + 2) * 32);
+    cfg.blockDim = dim3((CW + 2) * 32);
     cfg.dynamicSmemBytes = L::kAlloc;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1285,15 +1298,15 @@ cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensor
     return cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
 }
 
-template <typename T, int D, int NT, int NSTAGE>
+template <typename T, int D, int NT, int NSTAGE, int CW>
 int occupancy_t() {
-    using L = TcLayout<D, NT, NSTAGE>;
-    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE>;
+    using L = TcLayout<D, NT, NSTAGE, CW>;
+    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE, CW>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) !=
         cudaSuccess)
         return 0;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kConsumerWarps + 2) * 32,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (CW + 2) * 32,
                                                       L::kAlloc) != cudaSuccess)
         return 0;
     return n;
@@ -1310,24 +1323,32 @@ int occupancy_t() {
 #endif
 constexpr int kStages64 = TLB_ATTN_STAGES_64;
 constexpr int kStages128 = TLB_ATTN_STAGES_128;
+// Consumer warps of the one-head-tile kernels (the two-tile ones, group > 8,
+// need more registers per thread and keep kConsumerWarps).
+#ifndef TLB_ATTN_CW1
+#define TLB_ATTN_CW1 4
+#endif
+constexpr int kCw1 = TLB_ATTN_CW1;
 
 template <typename T>
 cudaError_t dispatch_tc(int head_dim, int group, const TcParams& p, const CUtensorMap& tk,
                         const CUtensorMap& tv, int grid, bool ov, cudaStream_t st) {
     const bool two = group > 8;
     if (head_dim == 64)
-        return two ? launch_tc_t<T, 64, 2, kStages64>(p, tk, tv, grid, ov, st)
-                   : launch_tc_t<T, 64, 1, kStages64>(p, tk, tv, grid, ov, st);
-    return two ? launch_tc_t<T, 128, 2, kStages128>(p, tk, tv, grid, ov, st)
-               : launch_tc_t<T, 128, 1, kStages128>(p, tk, tv, grid, ov, st);
+        return two ? launch_tc_t<T, 64, 2, kStages64, kConsumerWarps>(p, tk, tv, grid, ov, st)
+                   : launch_tc_t<T, 64, 1, kStages64, kCw1>(p, tk, tv, grid, ov, st);
+    return two ? launch_tc_t<T, 128, 2, kStages128, kConsumerWarps>(p, tk, tv, grid, ov, st)
+               : launch_tc_t<T, 128, 1, kStages128, kCw1>(p, tk, tv, grid, ov, st);
 }
 
 template <typename T>
 int occupancy_dispatch(int head_dim, int group) {
     const bool two = group > 8;
     if (head_dim == 64)
-        return two ? occupancy_t<T, 64, 2, kStages64>() : occupancy_t<T, 64, 1, kStages64>();
-    return two ? occupancy_t<T, 128, 2, kStages128>() : occupancy_t<T, 128, 1, kStages128>();
+        return two ? occupancy_t<T, 64, 2, kStages64, kConsumerWarps>()
+                   : occupancy_t<T, 64, 1, kStages64, kCw1>();
+    return two ? occupancy_t<T, 128, 2, kStages128, kConsumerWarps>()
+               : occupancy_t<T, 128, 1, kStages128, kCw1>();
 }
 
 template <typename T, int NPL>
