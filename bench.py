@@ -564,8 +564,14 @@ def run_sweep(args, rank, world, local):
         local_spec = W.DecodeSpec(spec.name, mine, spec.num_heads, spec.num_kv_heads,
                                   spec.head_dim, spec.block_size, spec.dtype,
                                   seed=spec.seed + rank)
+        # enough independent pools that one pass over them exceeds twice the
+        # 126 MB L2, so every launch reads its KV from HBM
+        e = 2 if spec.dtype != "float32" else 4
+        per_layer = R.attention_bytes(mine, spec.block_size, spec.num_heads, spec.num_kv_heads,
+                                      spec.head_dim, e)
+        nl = int(min(64, max(2, math.ceil(300e6 / max(per_layer, 1)))))
         layers = [W.make_batch(W.DecodeSpec(**{**local_spec.__dict__, "seed": local_spec.seed + 7 * l}),
-                               device=dev) for l in range(2)]
+                               device=dev) for l in range(nl)]
         stream = torch.cuda.Stream(dev)
 
         def attn():
@@ -584,7 +590,7 @@ def run_sweep(args, rank, world, local):
         stream.synchronize()
         if world > 1:
             dist.barrier(device_ids=[local])
-        reps = 50
+        reps = max(5, 200 // nl)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             e0.record(stream)
@@ -597,10 +603,8 @@ def run_sweep(args, rank, world, local):
             t = torch.tensor([ms], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = t.item()
-        e = 2 if spec.dtype != "float32" else 4
-        byt = R.attention_bytes(mine, spec.block_size, spec.num_heads, spec.num_kv_heads,
-                                spec.head_dim, e)
-        line = {"point": spec.name, "n_gpus": world, "tokens_per_s": round(len(glob) / (ms / 1e3), 1),
+        byt = per_layer
+        line = {"point": spec.name, "pools": nl, "n_gpus": world, "tokens_per_s": round(len(glob) / (ms / 1e3), 1),
                 "us_per_launch": round(ms * 1e3, 2),
                 "hbm_gbs_per_gpu": round(byt / (ms / 1e3) / 1e9, 1),
                 "frac_of_measured_peak": round(byt / (ms / 1e3) / 1e9 / peak, 4),

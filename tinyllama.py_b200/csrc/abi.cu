@@ -271,7 +271,7 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
         p.group = group;
         p.block_size = (int)block_size;
         p.max_blocks = (int)max_blocks_per_seq;
-        p.min_tokens = 512;
+        p.min_tokens = TLB_ATTN_MIN_TOKENS;
         p.scale_log2 = scale_log2;
         e = tlb::attn::launch_tc(dtype, (int)head_dim, group, p, tk, tv, grid,
                                  (flags & TLB_ATTN_OVERLAP_PROLOGUE) != 0, st);

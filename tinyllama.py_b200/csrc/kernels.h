@@ -23,6 +23,12 @@ constexpr int kGMax = 16;           // largest query-head group on the tensor-co
 // Persistent grid: at most this many CTAs per SM (also sizes the workspace).
 constexpr int kMaxCtasPerSm = TLB_ATTN_CTAS_PER_SM;
 constexpr int kWorkspaceHeader = 256;
+// Fewest context tokens (per kv head) a CTA of the tensor-core path is given
+// before another CTA joins: below this, a split's merge costs more than the
+// parallelism saves.
+#ifndef TLB_ATTN_MIN_TOKENS
+#define TLB_ATTN_MIN_TOKENS 128
+#endif
 // Work items per CTA of the grid the partial-result slots are sized for: one
 // static range per CTA plus at most two tail chunks per CTA.
 constexpr int kItemsPerCta = 3;

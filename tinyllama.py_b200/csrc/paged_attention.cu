@@ -72,6 +72,10 @@ constexpr int kItemCache = 512; // range starts kept in shared memory (grids up 
 // stages. Stage i of a unit sits at cost kCostPiece + kCostStage * i from the
 // unit's start; a range owns the stages whose cost point lies inside it.
 constexpr int kCostStage = 4;
+#ifndef TLB_ATTN_MAX_SPLITS
+#define TLB_ATTN_MAX_SPLITS 16
+#endif
+constexpr int kMaxSplits = TLB_ATTN_MAX_SPLITS;  // most pieces a (sequence, kv head) is cut into
 constexpr int kCostPiece = 5;
 #ifndef TLB_ATTN_PREFETCH
 #define TLB_ATTN_PREFETCH 3
@@ -310,7 +314,12 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     const long long Ws = (cached && kTailDen > 0) ? W - W / (kTailDen > 0 ? kTailDen : 1) : W;
     int P = (int)gridDim.x;
     {
-        const long long min_cost = (long long)max(1, p.min_tokens / ROWS) * kCS;
+        // Ranges of at least min_tokens, and long enough that a
+        // (sequence, kv head) of average cost is cut into at most kMaxSplits
+        // pieces: the last piece merges the others one pair at a time.
+        const long long avg_unit = W / ((long long)S * KVH);
+        const long long min_cost = max((long long)max(1, p.min_tokens / ROWS) * kCS,
+                                       (avg_unit + kMaxSplits - 1) / kMaxSplits);
         const long long want = (Ws + min_cost - 1) / min_cost;
         if (want < P) P = (int)(want > 0 ? want : 1);
     }
@@ -779,11 +788,10 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             auto slot_k = [&](int k) -> long long {
                 return 2ll * (e.jfirst + k) + ((k == 0 && e.first_slot1) ? 1 : 0);
             };
-            const bool fits = n * GP <= kCombineCap;
             unsigned seen = 0;
-            if (fits && lane == 0) seen = ld_acquire_gpu(p.counters + e.u);
+            if (lane == 0) seen = ld_acquire_gpu(p.counters + e.u);
             seen = __shfl_sync(0xffffffffu, seen, 0);
-            bool own_in_regs = fits && seen == (unsigned)(n - 1);
+            const bool own_in_regs = seen == (unsigned)(n - 1);
             if (own_in_regs) {
                 if (lane == 0) st_relaxed_gpu(p.counters + e.u, 0u);  // ready for the next launch
             } else {
@@ -810,96 +818,98 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 if (!last) continue;
             }
 
-            // Last piece of this (sequence, kv head) to finish: merge them all.
-            if (fits) {
-                // A piece that was not published keeps its partial in shared
-                // memory; every piece is then read the same way and summed in
-                // the same order (pairs, ascending), whichever came last, so
-                // the result is the same bits every run.
-                int own = -1;
-                if (own_in_regs) {
-                    for (int k = 0; k < n; ++k)
-                        if (slot_k(k) == e.slot) own = k;
+            // Last piece of this (sequence, kv head) to finish: merge them
+            // all. A piece that was not published keeps its partial in shared
+            // memory; every piece is read the same way and summed in the same
+            // order (pairs, ascending), whichever came last, so the result is
+            // the same bits every run. Pieces go through shared memory in
+            // chunks of kChunk; with more than one chunk the per-head maxima
+            // of all pieces are found first.
+            constexpr int kChunk = kCombineCap / GP;  // even: pairs never straddle chunks
+            static_assert(kChunk % 2 == 0, "combine chunks hold whole pairs");
+            float* sGM = sW;       // per-head max over all pieces
+            float* sGL = sW + GP;  // per-head weighted sum of l (its reciprocal at the end)
+            int own = -1;
+            if (own_in_regs) {
+                for (int k = 0; k < n; ++k)
+                    if (slot_k(k) == e.slot) own = k;
 #pragma unroll
-                    for (int i = 0; i < kPer4; ++i)
-                        *reinterpret_cast<float4*>(sOwn + 4 * (lane + 32 * i)) = acc[i];
-                }
-                for (int idx = lane; idx < n * G; idx += 32) {
-                    const int k = idx / G, h = idx - (idx / G) * G;
-                    float2 ml;
-                    if (k == own) {
-                        ml = make_float2(sHM[h], sHL[h]);
-                    } else {
-                        ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot_k(k) * GP + h) * 2));
-                    }
-                    sCW[k * GP + h] = ml.x;
-                    sCL[k * GP + h] = ml.y;
-                }
-                auto load_piece = [&](int k, int i) -> float4 {
-                    const int el = 4 * (lane + 32 * i);
-                    if (el / D >= G) return make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (k == own) return *reinterpret_cast<const float4*>(sOwn + el);
-                    return __ldcg(reinterpret_cast<const float4*>(p.ws_o + slot_k(k) * GP * D + el));
-                };
+                for (int i = 0; i < kPer4; ++i)
+                    *reinterpret_cast<float4*>(sOwn + 4 * (lane + 32 * i)) = acc[i];
+            }
+            auto m_of = [&](int k, int h) -> float2 {
+                if (k == own) return make_float2(sHM[h], sHL[h]);
+                return __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot_k(k) * GP + h) * 2));
+            };
+            const bool one_chunk = n <= kChunk;
+            if (!one_chunk) {
+                for (int h = 0; h < G; ++h) {
+                    float mx = -INFINITY;
+                    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, m_of(k, h).x);
 #pragma unroll
-                for (int i = 0; i < kPer4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int k = 0; k < n; k += 2) {
-                    const bool two = k + 1 < n;
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    if (lane == 0) sGM[h] = mx;
+                }
+            }
+            auto load_piece = [&](int k, int i) -> float4 {
+                const int el = 4 * (lane + 32 * i);
+                if (el / D >= G) return make_float4(0.f, 0.f, 0.f, 0.f);
+                if (k == own) return *reinterpret_cast<const float4*>(sOwn + el);
+                return __ldcg(reinterpret_cast<const float4*>(p.ws_o + slot_k(k) * GP * D + el));
+            };
+#pragma unroll
+            for (int i = 0; i < kPer4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c0 = 0; c0 < n; c0 += kChunk) {
+                const int cn = min(kChunk, n - c0);
+                __syncwarp();
+                for (int idx = lane; idx < cn * G; idx += 32) {
+                    const int kk = idx / G, h = idx - (idx / G) * G;
+                    const float2 ml = m_of(c0 + kk, h);
+                    sCW[kk * GP + h] = ml.x;
+                    sCL[kk * GP + h] = ml.y;
+                }
+                for (int kk = 0; kk < cn; kk += 2) {
+                    const bool two = kk + 1 < cn;
                     float4 v0[kPer4], v1[kPer4];
 #pragma unroll
                     for (int i = 0; i < kPer4; ++i) {
-                        v0[i] = load_piece(k, i);
-                        v1[i] = two ? load_piece(k + 1, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        v0[i] = load_piece(c0 + kk, i);
+                        v1[i] = two ? load_piece(c0 + kk + 1, i) : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
-                    if (k == 0) {  // weights, while the first two pieces load
+                    if (kk == 0) {  // the chunk's weights, while its first pair loads
                         __syncwarp();
                         if (lane < G) {
-                            float M = -INFINITY;
-                            for (int kk = 0; kk < n; ++kk) M = fmaxf(M, sCW[kk * GP + lane]);
-                            float lt = 0.f;
-                            for (int kk = 0; kk < n; ++kk) {
-                                const float wt =
-                                    M == -INFINITY ? 0.f : exp2f(sCW[kk * GP + lane] - M);
-                                sCW[kk * GP + lane] = wt;
-                                lt += wt * sCL[kk * GP + lane];
+                            float M = one_chunk ? -INFINITY : sGM[lane];
+                            if (one_chunk)
+                                for (int j = 0; j < cn; ++j) M = fmaxf(M, sCW[j * GP + lane]);
+                            float lt = c0 == 0 ? 0.f : sGL[lane];
+                            for (int j = 0; j < cn; ++j) {
+                                const float wt = M == -INFINITY ? 0.f : exp2f(sCW[j * GP + lane] - M);
+                                sCW[j * GP + lane] = wt;
+                                lt += wt * sCL[j * GP + lane];
                             }
-                            sHL[lane] = lt > 0.f ? 1.f / lt : 0.f;
+                            // after the last chunk: the reciprocal, for the store
+                            sGL[lane] = c0 + cn < n ? lt : (lt > 0.f ? 1.f / lt : 0.f);
                         }
                         __syncwarp();
                     }
 #pragma unroll
                     for (int i = 0; i < kPer4; ++i) {
                         const int h = min(4 * (lane + 32 * i) / D, GP - 1);
-                        const float w0 = sCW[k * GP + h], w1 = two ? sCW[(k + 1) * GP + h] : 0.f;
+                        const float w0 = sCW[kk * GP + h], w1 = two ? sCW[(kk + 1) * GP + h] : 0.f;
                         acc[i].x += w0 * v0[i].x + w1 * v1[i].x;
                         acc[i].y += w0 * v0[i].y + w1 * v1[i].y;
                         acc[i].z += w0 * v0[i].z + w1 * v1[i].z;
                         acc[i].w += w0 * v0[i].w + w1 * v1[i].w;
                     }
                 }
-#pragma unroll
-                for (int i = 0; i < kPer4; ++i) {
-                    const int h = 4 * (lane + 32 * i) / D;
-                    if (h < G) store_out(i, sHL[h]);
-                }
-                __syncwarp();
-            } else {
-                for (int el = lane; el < G * D; el += 32) {
-                    const int h = el / D;
-                    float M = -INFINITY;
-                    for (int k = 0; k < n; ++k)
-                        M = fmaxf(M, __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2));
-                    float a = 0.f, lt = 0.f;
-                    if (M != -INFINITY) {
-                        for (int k = 0; k < n; ++k) {
-                            const float wt = exp2f(__ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2) - M);
-                            a += wt * __ldcg(p.ws_o + slot_k(k) * GP * D + el);
-                            lt += wt * __ldcg(p.ws_ml + (slot_k(k) * GP + h) * 2 + 1);
-                        }
-                    }
-                    out[out_base + el] = Elem<T>::from_f(lt > 0.f ? a / lt : 0.f);
-                }
             }
+#pragma unroll
+            for (int i = 0; i < kPer4; ++i) {
+                const int h = 4 * (lane + 32 * i) / D;
+                if (h < G) store_out(i, sGL[h]);
+            }
+            __syncwarp();
         }
         return;
     }
@@ -1328,7 +1338,11 @@ constexpr int kStages128 = TLB_ATTN_STAGES_128;
 #ifndef TLB_ATTN_CW1
 #define TLB_ATTN_CW1 4
 #endif
-constexpr int kCw1 = TLB_ATTN_CW1;
+#ifndef TLB_ATTN_CW1_64
+#define TLB_ATTN_CW1_64 4
+#endif
+constexpr int kCw1 = TLB_ATTN_CW1;        // head_dim 128
+constexpr int kCw1_64 = TLB_ATTN_CW1_64;  // head_dim 64
 
 template <typename T>
 cudaError_t dispatch_tc(int head_dim, int group, const TcParams& p, const CUtensorMap& tk,
@@ -1336,7 +1350,7 @@ cudaError_t dispatch_tc(int head_dim, int group, const TcParams& p, const CUtens
     const bool two = group > 8;
     if (head_dim == 64)
         return two ? launch_tc_t<T, 64, 2, kStages64, kConsumerWarps>(p, tk, tv, grid, ov, st)
-                   : launch_tc_t<T, 64, 1, kStages64, kCw1>(p, tk, tv, grid, ov, st);
+                   : launch_tc_t<T, 64, 1, kStages64, kCw1_64>(p, tk, tv, grid, ov, st);
     return two ? launch_tc_t<T, 128, 2, kStages128, kConsumerWarps>(p, tk, tv, grid, ov, st)
                : launch_tc_t<T, 128, 1, kStages128, kCw1>(p, tk, tv, grid, ov, st);
 }
@@ -1346,7 +1360,7 @@ int occupancy_dispatch(int head_dim, int group) {
     const bool two = group > 8;
     if (head_dim == 64)
         return two ? occupancy_t<T, 64, 2, kStages64, kConsumerWarps>()
-                   : occupancy_t<T, 64, 1, kStages64, kCw1>();
+                   : occupancy_t<T, 64, 1, kStages64, kCw1_64>();
     return two ? occupancy_t<T, 128, 2, kStages128, kConsumerWarps>()
                : occupancy_t<T, 128, 1, kStages128, kCw1>();
 }
