@@ -86,6 +86,16 @@ def global_lengths(n_gpus: int, seed: int):
     return W.qwen3b_decode(seed, batch=64 * n_gpus).seq_lens
 
 
+def lpt_balance(world: int, seed: int) -> float:
+    """Largest GPU's context tokens over the mean: the ideal-bound factor of
+    the weak-scaling split (1.0 = perfectly balanced)."""
+    from paged_decode import partition as P
+
+    lens = global_lengths(world, seed)
+    loads = P.shard_loads(lens, P.lpt_assign(lens, world))
+    return round(max(loads) / (sum(loads) / world), 4)
+
+
 def rank_spec(rank: int, world: int, seed: int, layer: int):
     from paged_decode import partition as P
     from paged_decode import workloads as W
@@ -278,6 +288,25 @@ def run_ours(args, rank, world, local):
         sampler.__exit__(None, None, None)
     attn_ms = timed(g_attn, reps)
 
+    # spread: 20 samples of the step, each over a slice of the replays
+    nsamp = 20
+    per = max(1, reps // nsamp)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(nsamp + 1)]
+    with torch.cuda.stream(stream):
+        evs[0].record(stream)
+        for i in range(nsamp):
+            for _ in range(per):
+                g_step.replay()
+            evs[i + 1].record(stream)
+    torch.cuda.synchronize(dev)
+    samp = torch.tensor([evs[i].elapsed_time(evs[i + 1]) * 1e3 / (per * nl) for i in range(nsamp)],
+                        dtype=torch.float64)
+    if world > 1:
+        samp = samp.to(dev)
+        dist.all_reduce(samp, op=dist.ReduceOp.MAX)
+        samp = samp.cpu()
+    q10, q50, q90 = (float(torch.quantile(samp, q)) for q in (0.1, 0.5, 0.9))
+
     # ---- end to end through the public ops, host buffers each step
     e2e = None
     if not args.no_e2e:
@@ -307,6 +336,7 @@ def run_ours(args, rank, world, local):
         "data": "synthetic (seeded N(0,1) q/k/v and KV pool, seeded lengths)",
         "config": {"workload": WORKLOAD, "global_batch": tokens_per_step, "seq_len": "U[128,4096]",
                    "parallelism": f"sequence-sharded x{world} (LPT), no collective",
+                   "lpt_max_load_over_mean": lpt_balance(world, args.seed),
                    "l2": f"{nl} rotating independent KV pools per GPU "
                          f"(~{nl * attn_bytes / 1e6:.0f} MB of KV per rotation > 126 MB L2)",
                    "timed_region": "CUDA-graph replay of fused RoPE+cache-write + paged attention"},
@@ -320,6 +350,7 @@ def run_ours(args, rank, world, local):
                      "algorithmic_bytes_per_launch": int(attn_bytes),
                      "launch_us": round(t_attn_us, 3),
                      "traffic": traffic},
+        "step_us_p10_p50_p90": [round(q10, 3), round(q50, 3), round(q90, 3)],
         "gpu_launches": 2 * steps * world,
         "gpu_launches_per_rank": 2 * steps,
         "clocks": sampler.summary() if sampler else None,
@@ -490,6 +521,17 @@ def oracle_step(inp, seqs, threads):
                                      inp["scale"], "bfloat16", threads)
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(batch, seconds):
     cores = os.cpu_count() or 1
     inp = oracle_inputs(batch)
@@ -505,6 +547,7 @@ def cpu_baseline(batch, seconds):
         if el >= seconds and done >= S:
             break
     return {"value": round(done / el, 2), "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_model": cpu_model(),
             "sample": f"CPU oracle (numpy, {cores} threads) over {done} sequences of the same "
                       f"workload in chunks of {chunk}, {el:.1f} s"}
 
@@ -535,6 +578,7 @@ def run_reference(args, rank, world):
         "config": {"workload": WORKLOAD, "global_batch": 64,
                    "sample_per_step": f"{chunk} of the 64 sequences (rotating)"},
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                         "cpu_model": cpu_model(),
                          "sample": f"each step: RoPE + cache write + attention of {chunk} "
                                    f"sequences, CPU oracle (numpy, {cores} threads)"},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
