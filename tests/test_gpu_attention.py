@@ -221,3 +221,23 @@ def test_cpu_tensor_raises_reference_message():
     with pytest.raises(RuntimeError, match="query must be a CUDA tensor"):
         A.paged_attention(q, q.view(1, 2, 1, 64), q.view(1, 2, 1, 64),
                           torch.zeros(1, 1, dtype=torch.int32), torch.ones(1, dtype=torch.int32), 1.0)
+
+
+@pytest.mark.parametrize("H,KVH,D,bs,lens", [
+    (14, 2, 64, 8, [512]),                       # one sequence cut into many pieces
+    (16, 2, 128, 16, [512]),
+    (14, 2, 64, 16, [1, 2, 15, 16, 17, 100, 333, 1024, 0, 77]),
+    (16, 1, 128, 64, [4096, 3, 700]),
+    (32, 2, 128, 32, [8192, 9, 2000]),             # two head tiles (group 16)
+])
+def test_counters_are_zero_after_every_launch(H, KVH, D, bs, lens, built_lib):
+    """Split pieces meet on per-(sequence, kv head) arrival counters that every
+    launch must leave at zero; a count that never completes would corrupt the
+    next launch on the same stream."""
+    batch = _custom_batch(lens, H, KVH, D, bs, "bfloat16")
+    for _ in range(3):
+        out = _attend(batch)
+        check_attention(batch, out)
+    torch.cuda.synchronize()
+    ws = A._workspaces[(torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream)]
+    assert ws.clean > 0 and int(ws.buf[:ws.clean].count_nonzero()) == 0

@@ -110,9 +110,16 @@ struct alignas(8) Job {
     int valid;
 };
 
+#ifndef TLB_ATTN_TPW64
+#define TLB_ATTN_TPW64 2
+#endif
 template <int D, int NT, int NSTAGE, int CW>
 struct TcLayout {
-    static constexpr int kRows = CW * kTileRows;      // tokens per stage
+    // 16-token tiles each consumer warp takes per stage: head dim 64 takes two,
+    // so a stage carries as many bytes (32 KB of K and V) as with head dim 128
+    // and the per-stage costs are paid once per 32 KB either way.
+    static constexpr int kTpw = D == 64 ? TLB_ATTN_TPW64 : 1;
+    static constexpr int kRows = CW * kTileRows * kTpw;  // tokens per stage
     static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
     static constexpr int kStageKV = kRows * D * 2;  // bytes of K (or V) per stage
     static constexpr int kQBytes = 8 * NT * D * 2;     // query group of the piece
@@ -318,14 +325,17 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         // (sequence, kv head) of average cost is cut into at most kMaxSplits
         // pieces: the last piece merges the others one pair at a time.
         const long long avg_unit = W / ((long long)S * KVH);
+        // Every range is at least one stage's cost long, so a range inside a
+        // unit always holds a stage point and each piece count (nsplits) is
+        // exact: ranges are floor(Ws / P) or longer.
         const long long min_cost = max((long long)max(1, p.min_tokens / ROWS) * kCS,
                                        (avg_unit + kMaxSplits - 1) / kMaxSplits);
-        const long long want = (Ws + min_cost - 1) / min_cost;
+        const long long want = Ws / min_cost;
         if (want < P) P = (int)(want > 0 ? want : 1);
     }
     const long long Wt = W - Ws;
     long long C = (Wt + 2ll * gridDim.x - 1) / (2ll * gridDim.x);
-    if (C < 4) C = 4;
+    if (C < kCS) C = kCS;  // a chunk holds at least one stage point
     const int T_tail = (int)((Wt + C - 1) / C);
     // Range starts go to shared memory once (one 64-bit division per
     // entry, spread over the block), so the producer's per-piece lookups
@@ -920,13 +930,18 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     const uint32_t mi = lane >> 3;
     const int ld_row = (lane & 7) + ((mi >> 1) << 3);  // ldmatrix row within a 16-row tile
     const int ld_kk = (int)(mi & 1);
-    const int r0 = warp * kTileRows;
-    // Stage row r lives in block tile r / bs at row r % bs; chunk c of a tile
-    // starts c * bs * 128 bytes in. Row offset of this lane's ldmatrix row:
-    const int ld_r = r0 + ld_row;
-    const uint32_t ld_off = (uint32_t)((ld_r / bs) * (bs * D * 2) + (ld_r % bs) * 128);
+    constexpr int TPW = L::kTpw;
+    // Tile t of this warp is stage rows [(t * CW + warp) * 16, +16). Stage row
+    // r lives in block tile r / bs at row r % bs; chunk c of a tile starts
+    // c * bs * 128 bytes in. Row offset of this lane's ldmatrix row per tile:
+    uint32_t ld_off_t[TPW];
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+        const int ld_r = (t * CW + warp) * kTileRows + ld_row;
+        ld_off_t[t] = (uint32_t)((ld_r / bs) * (bs * D * 2) + (ld_r % bs) * 128);
+    }
     const uint32_t chunk_bytes = (uint32_t)(bs * 128);
-    const int ld_swz = ld_r & 7;  // bs is a multiple of 8: the row's place in its swizzle atom
+    const int ld_swz = ld_row & 7;  // bs and tile starts are multiples of 8
 
     float m_run[2], l_run[2];
     float o[NT][KS][4];
@@ -968,7 +983,11 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             l_run[0] = l_run[1] = 0.f;
         }
 
-        // Valid rows of this warp's 16-token tile.
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+        const int r0 = (t * CW + warp) * kTileRows;
+        const uint32_t ld_off = ld_off_t[t];
+        // Valid rows of this 16-token tile.
         const unsigned vmask = (sDesc[stage].rows[r0 >> 5] >> (r0 & 31)) & 0xffffu;
 
         if (vmask != 0u) {
@@ -1109,6 +1128,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                         mma16816<T>(o[nt][mt], vf[mt], pl[nt][0], pl[nt][1]);
             }
         }
+        }  // tiles of this warp
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
         if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
@@ -1326,7 +1346,7 @@ int occupancy_t() {
 // stages (K, V and the query group) in flight, ~160 KB per SM, enough to
 // cover HBM latency under full load (bytes in flight = bandwidth x latency).
 #ifndef TLB_ATTN_STAGES_64
-#define TLB_ATTN_STAGES_64 4
+#define TLB_ATTN_STAGES_64 (TLB_ATTN_TPW64 == 2 ? 2 : 4)
 #endif
 #ifndef TLB_ATTN_STAGES_128
 #define TLB_ATTN_STAGES_128 2
