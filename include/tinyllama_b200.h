@@ -151,6 +151,44 @@ TLB_API int tlb_paged_attention_no_alloc(void* out, const void* query, const voi
                         float scale, int dtype, unsigned flags, void* stream);
 
 /* ------------------------------------------------------------------------
+ * The decode step in one launch: NeoX RoPE on the query and key, the KV-cache
+ * write of the new token, and paged attention. It computes what
+ *   tlb_rotary_embedding_neox_with_cache(positions = seq_lens - 1, ...,
+ *       block_tables addressing, rot_dim = head_dim)
+ * followed by tlb_paged_attention on the rotated query computes
+ * (pos_encoding_kernel.cu:24-65, attention.py:96-116 and
+ * attention_kernel.cu:24-150 in that order; attention.py:151-166 is the layer
+ * that runs them), for a decode batch: one new token per sequence, at
+ * position seq_lens[s] - 1, so that token's row lies in the sequence's last
+ * block, which one CTA alone reads: that CTA rotates the key, stores it and
+ * the value into the caches, and then loads the block.
+ *
+ *   query  : [num_seqs, num_heads, head_dim] raw (not rotated), not modified
+ *   key    : [num_seqs, key_stride] raw key, rotated in place (as
+ *            tlb_rotary_embedding_neox leaves it)
+ *   value  : [num_seqs, value_stride]
+ *   cos_sin_cache : [cache_rows, head_dim] (cos | sin halves), query dtype
+ * Positions outside the table leave the vectors unrotated and set
+ * TLB_STATUS_BAD_POSITION; block ids outside the pool skip the write (and
+ * the read, TLB_STATUS_BAD_BLOCK_ID), negative ones skip both silently.
+ * Tensor-core shapes only (fp16/bf16, head_dim 64 or 128, group <= 16,
+ * block_size 8..64, 16-byte aligned tensors); others return
+ * TLB_ERR_UNSUPPORTED and are served by the two calls above. Workspace and
+ * flags as tlb_paged_attention (TLB_ATTN_OVERLAP_PROLOGUE: the kernel before
+ * writes neither block_tables nor seq_lens nor the cos/sin table).
+ * No reference counterpart: a fusion of the three reference steps.
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_paged_attention_with_rope(void* out, const void* query, void* key,
+                        const void* value, void* key_cache, void* value_cache,
+                        const int32_t* block_tables, const int32_t* seq_lens,
+                        const void* cos_sin_cache, int64_t cache_rows,
+                        int64_t num_seqs, int64_t num_heads, int64_t num_kv_heads,
+                        int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                        int64_t max_blocks_per_seq, int64_t key_stride,
+                        int64_t value_stride, float scale, int dtype, void* workspace,
+                        size_t workspace_bytes, unsigned flags, void* stream);
+
+/* ------------------------------------------------------------------------
  * NeoX rotary embedding.
  *
  * Replaces `rotary_embedding_neox(postions, query, key, head_size,

@@ -18,6 +18,7 @@ LIB_NAME = "libtinyllama_b200.so"
 LIB_PATH = Path(__file__).resolve().with_name(LIB_NAME)
 
 TLB_OK = 0
+TLB_ERR_UNSUPPORTED = 2
 DTYPE_CODE = {
     torch.float32: 0,
     torch.float16: 1,
@@ -43,6 +44,9 @@ _PROTOS = {
                             _i64, _f32, _i32, _vp, _sz, ctypes.c_uint, _vp],
     "tlb_paged_attention_no_alloc": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                      _i64, _i64, _f32, _i32, ctypes.c_uint, _vp],
+    "tlb_paged_attention_with_rope": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                      _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32,
+                                      _vp, _sz, ctypes.c_uint, _vp],
     "tlb_rotary_embedding_neox": [_vp, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64,
                                   _i64, _i64, _i64, _i64, _i32, _vp],
     "tlb_reshape_and_cache": [_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -140,3 +140,77 @@ def paged_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: t
             ws.numel() if ws is not None else 0, 1 if overlap_prologue else 0, stream)
         _lib.check(rc)
     return out
+
+
+def paged_attention_with_rope(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                              key_cache: torch.Tensor, value_cache: torch.Tensor,
+                              block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                              cos_sin_cache: torch.Tensor, scale: float, *,
+                              overlap_prologue: bool = False) -> torch.Tensor:
+    """A decode step in one launch (not in the reference API): NeoX RoPE of the
+    raw ``query`` and ``key`` at position ``seq_lens[s] - 1``, the cache write
+    of that token's rotated key and ``value`` through ``block_tables``, and
+    paged attention with the rotated query — what
+    ``rotary_embedding_neox_with_cache(seq_lens - 1, query, key, value, ...,
+    block_tables=block_tables)`` followed by ``paged_attention`` computes
+    (src/model_executor/layers/attention.py:151-166 for a decode batch).
+
+    query [num_seqs, num_heads, head_dim] (left as is), key
+    [num_seqs, num_kv_heads * head_dim] or [num_seqs, num_kv_heads, head_dim]
+    (rotated in place), value likewise, cos_sin_cache [rows, head_dim] in the
+    query dtype. Shapes the tensor-core kernel does not serve run as those two
+    launches.
+    """
+    torch_check(query.is_cuda and key.is_cuda and value.is_cuda and cos_sin_cache.is_cuda,
+                "query, key, value and cos_sin_cache must be CUDA tensors")
+    torch_check(query.dim() == 3 and query.is_contiguous(),
+                "query must be a contiguous [num_seqs, num_heads, head_dim] tensor")
+    num_seqs, num_heads, head_dim = query.shape
+    k2 = key.reshape(num_seqs, -1) if key.dim() == 3 else key
+    v2 = value.reshape(num_seqs, -1)
+    torch_check(k2.dim() == 2 and k2.size(0) == num_seqs and k2.stride(1) == 1,
+                "key must be [num_seqs, num_kv_heads * head_dim] with unit inner stride")
+    torch_check(v2.size(1) == k2.size(1) and v2.stride(1) == 1,
+                "value must match key: [num_seqs, num_kv_heads, head_dim]")
+    torch_check(key.dtype == query.dtype and value.dtype == query.dtype
+                and cos_sin_cache.dtype == query.dtype,
+                "key, value and cos_sin_cache must share the query dtype")
+    torch_check(cos_sin_cache.dim() == 2 and cos_sin_cache.is_contiguous()
+                and cos_sin_cache.size(1) == head_dim,
+                "cos_sin_cache must be a contiguous [rows, head_dim] tensor")
+    torch_check(key_cache.dim() == 4 and k2.size(1) == key_cache.size(1) * head_dim,
+                "key must hold num_kv_heads * head_dim values per token")
+    torch_check(seq_lens.dim() == 1 and seq_lens.size(0) == num_seqs,
+                "seq_lens must have one entry per sequence")
+    out = torch.empty_like(query)
+    if key_cache.size(0) > 0 and block_tables.dim() == 2 and block_tables.size(1) > 0 \
+            and block_tables.dtype == torch.int32 and seq_lens.dtype == torch.int32 \
+            and block_tables.is_contiguous() and seq_lens.is_contiguous() \
+            and key_cache.is_contiguous() and value_cache.is_contiguous() \
+            and key_cache.shape == value_cache.shape and key_cache.dtype == query.dtype:
+        lib = _lib.load()
+        dev = query.device
+        with _lib.device_guard(dev):
+            stream = _lib.stream_of(dev)
+            nbytes, zeroed = workspace_bytes(num_seqs, num_heads, key_cache.size(1), head_dim,
+                                             query.dtype, dev.index)
+            ws = _workspace(dev, stream, nbytes, zeroed)
+            rc = lib.tlb_paged_attention_with_rope(
+                out.data_ptr(), query.data_ptr(), k2.data_ptr(), v2.data_ptr(),
+                key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+                seq_lens.data_ptr(), cos_sin_cache.data_ptr(), cos_sin_cache.size(0), num_seqs,
+                num_heads, key_cache.size(1), head_dim, key_cache.size(0), key_cache.size(2),
+                block_tables.size(1), k2.stride(0), v2.stride(0), float(scale),
+                DTYPE_CODE[query.dtype], ws.data_ptr() if ws is not None else None,
+                ws.numel() if ws is not None else 0, 1 if overlap_prologue else 0, stream)
+            if rc != _lib.TLB_ERR_UNSUPPORTED:
+                _lib.check(rc)
+                return out
+    # Shapes outside the fused kernel: the same step as two launches.
+    from . import pos_encoding as _PE
+    positions = (seq_lens.to(torch.int64) - 1)
+    q_rot = _PE.rotary_embedding_neox_with_cache(
+        positions, query.reshape(num_seqs, -1), k2, v2, key_cache, value_cache, None, head_dim,
+        cos_sin_cache, block_tables=block_tables)
+    return paged_attention(q_rot.view(num_seqs, num_heads, head_dim), key_cache, value_cache,
+                           block_tables, seq_lens, scale)

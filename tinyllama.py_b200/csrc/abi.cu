@@ -208,13 +208,23 @@ int tlb_paged_attention_workspace_zeroed_bytes(int64_t num_seqs, int64_t num_kv_
     return TLB_OK;
 }
 
-int tlb_paged_attention(void* out, const void* query, const void* key_cache,
-                        const void* value_cache, const int32_t* block_tables,
-                        const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
-                        int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
-                        int64_t block_size, int64_t max_blocks_per_seq, float scale, int dtype,
-                        void* workspace, size_t workspace_bytes, unsigned flags,
-                        void* stream) {
+namespace {
+// The decode step's RoPE and cache write, folded into the attention launch.
+struct FusedRope {
+    const void* cos_sin;
+    int64_t cache_rows;
+    void* key;
+    const void* value;
+    int64_t key_stride, value_stride;
+};
+
+int attention_impl(void* out, const void* query, const void* key_cache,
+                   const void* value_cache, const int32_t* block_tables,
+                   const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
+                   int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                   int64_t block_size, int64_t max_blocks_per_seq, float scale, int dtype,
+                   void* workspace, size_t workspace_bytes, unsigned flags, void* stream,
+                   const FusedRope* fr) {
     TLB_REQUIRE(is_float(dtype), "dtype must be float16, bfloat16 or float32");
     TLB_REQUIRE((flags & ~TLB_ATTN_OVERLAP_PROLOGUE) == 0, "unknown flags");
     TLB_REQUIRE(num_seqs > 0, "query must contain at least one sequence");
@@ -239,6 +249,10 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
     const bool tc = tlb::attn::tc_supported(dtype, (int)head_dim, group, (int)block_size) &&
                     aligned(query, 16) && aligned(key_cache, 16) && aligned(value_cache, 16) &&
                     rows < (1ull << 31);
+    if (fr != nullptr && !(tc && aligned(fr->cos_sin, 16)))
+        return fail(TLB_ERR_UNSUPPORTED,
+                    "the fused decode step needs the tensor-core path (fp16/bf16, head_dim 64 "
+                    "or 128, group <= 16, block_size 8..64, 16-byte aligned tensors)");
     if (tc) {
         int dev;
         if (int rc = current_device(&dev)) return rc;
@@ -254,7 +268,7 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
         CUtensorMap tk, tv;
         if (int rc = kv_tensor_map(key_cache, rows, (int)head_dim, (int)block_size, &tk)) return rc;
         if (int rc = kv_tensor_map(value_cache, rows, (int)head_dim, (int)block_size, &tv)) return rc;
-        tlb::attn::TcParams p;
+        tlb::attn::TcParams p{};
         char* ws = static_cast<char*>(workspace);
         p.out = out;
         p.query = query;
@@ -273,6 +287,16 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
         p.max_blocks = (int)max_blocks_per_seq;
         p.min_tokens = TLB_ATTN_MIN_TOKENS;
         p.scale_log2 = scale_log2;
+        if (fr != nullptr) {
+            p.cos_sin = fr->cos_sin;
+            p.cache_rows = fr->cache_rows;
+            p.key_new = fr->key;
+            p.value_new = fr->value;
+            p.key_stride = fr->key_stride;
+            p.value_stride = fr->value_stride;
+            p.key_cache = const_cast<void*>(key_cache);
+            p.value_cache = const_cast<void*>(value_cache);
+        }
         e = tlb::attn::launch_tc(dtype, (int)head_dim, group, p, tk, tv, grid,
                                  (flags & TLB_ATTN_OVERLAP_PROLOGUE) != 0, st);
         if (e != cudaSuccess) return cuda_fail(e, "launching paged attention");
@@ -297,6 +321,43 @@ int tlb_paged_attention(void* out, const void* query, const void* key_cache,
     cudaError_t e = tlb::attn::launch_generic(dtype, g, st);
     if (e != cudaSuccess) return cuda_fail(e, "launching paged attention");
     return TLB_OK;
+}
+}  // namespace
+
+int tlb_paged_attention(void* out, const void* query, const void* key_cache,
+                        const void* value_cache, const int32_t* block_tables,
+                        const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
+                        int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                        int64_t block_size, int64_t max_blocks_per_seq, float scale, int dtype,
+                        void* workspace, size_t workspace_bytes, unsigned flags,
+                        void* stream) {
+    return attention_impl(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs,
+                          num_heads, num_kv_heads, head_dim, num_blocks, block_size,
+                          max_blocks_per_seq, scale, dtype, workspace, workspace_bytes, flags,
+                          stream, nullptr);
+}
+
+int tlb_paged_attention_with_rope(void* out, const void* query, void* key, const void* value,
+                                  void* key_cache, void* value_cache,
+                                  const int32_t* block_tables, const int32_t* seq_lens,
+                                  const void* cos_sin_cache, int64_t cache_rows,
+                                  int64_t num_seqs, int64_t num_heads, int64_t num_kv_heads,
+                                  int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                  int64_t max_blocks_per_seq, int64_t key_stride,
+                                  int64_t value_stride, float scale, int dtype, void* workspace,
+                                  size_t workspace_bytes, unsigned flags, void* stream) {
+    TLB_REQUIRE(key && value && cos_sin_cache, "tensor pointers must not be null");
+    TLB_REQUIRE(cache_rows > 0, "cos_sin_cache must have at least one row");
+    TLB_REQUIRE(key_stride >= num_kv_heads * head_dim && value_stride >= num_kv_heads * head_dim,
+                "key / value rows are shorter than num_kv_heads * head_dim");
+    const int esz = is_float(dtype) ? elem_bytes(dtype) : 1;
+    TLB_REQUIRE(aligned(key, esz) && aligned(value, esz) && aligned(cos_sin_cache, esz),
+                "tensor pointers must be aligned to the element size");
+    const FusedRope fr{cos_sin_cache, cache_rows, key, value, key_stride, value_stride};
+    return attention_impl(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs,
+                          num_heads, num_kv_heads, head_dim, num_blocks, block_size,
+                          max_blocks_per_seq, scale, dtype, workspace, workspace_bytes, flags,
+                          stream, &fr);
 }
 
 // ---------------------------------------------------------------- rope etc.

@@ -101,6 +101,21 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders this thread's generic-proxy global stores before later async-proxy
+// (TMA) reads of the same addresses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// NeoX rotation of the pair (x, y) = (v[i], v[i + rot/2]) by (c, s) =
+// (cos_sin[pos, i], cos_sin[pos, rot/2 + i]) in fp32
+// (pos_encoding_kernel.cu:24-65). Every kernel that rotates goes through this
+// one expression, so they all round to the same bits.
+__device__ __forceinline__ void rope_pair(float x, float y, float c, float s, float& xo,
+                                          float& yo) {
+    xo = x * c - y * s;
+    yo = y * c + x * s;
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");

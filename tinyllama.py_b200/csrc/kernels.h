@@ -51,6 +51,19 @@ struct TcParams {
     int max_blocks;
     int min_tokens;           // fewest tokens (per kv head) a CTA is given before more join
     float scale_log2;         // softmax scale * log2(e)
+    // Fused decode step (cos_sin != nullptr): the new token of sequence s sits
+    // at position seq_lens[s] - 1. `query` is then the raw query, rotated in
+    // the kernel (NeoX, rot_dim == head_dim); the CTA that reads a sequence's
+    // last block first writes that kv head's rotated key and its value into
+    // the caches there (and the rotated key back into `key_new`).
+    const void* cos_sin;      // [cache_rows, head_dim]: cos | sin halves
+    long long cache_rows;
+    void* key_new;            // [num_seqs, key_stride] raw key, rotated in place
+    const void* value_new;    // [num_seqs, value_stride]
+    long long key_stride;     // elements between tokens
+    long long value_stride;
+    void* key_cache;          // the caches, for the new rows' stores
+    void* value_cache;
 };
 
 struct GenericParams {

@@ -47,6 +47,7 @@ enum : int {
     kPieceEnd = 2,
     kPieceComplete = 4,
     kTerminate = 8,
+    kRopeSkip = 16,  // fused step: the position is outside the cos/sin table, no rotation
 };
 
 // Written by the producer as three 16-byte stores.
@@ -108,6 +109,7 @@ struct alignas(8) Job {
     int item;        // work item the piece belongs to (partial slot 2*item + !first)
     int first;       // first piece of its item
     int valid;
+    int pos;         // position of the sequence's new token (its length - 1)
 };
 
 #ifndef TLB_ATTN_TPW64
@@ -122,7 +124,8 @@ struct TcLayout {
     static constexpr int kRows = CW * kTileRows * kTpw;  // tokens per stage
     static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
     static constexpr int kStageKV = kRows * D * 2;  // bytes of K (or V) per stage
-    static constexpr int kQBytes = 8 * NT * D * 2;     // query group of the piece
+    // query group of the piece, then (fused RoPE) the cos/sin row of its position
+    static constexpr int kQBytes = 8 * NT * D * 2 + D * 2;
     static constexpr int kGP = 8 * NT;                 // padded heads per piece
     static constexpr int kOFloats = CW * kGP * D;
     static constexpr int kOffK = 0;
@@ -133,7 +136,8 @@ struct TcLayout {
     static constexpr int kOffL = kOffM + CW * kGP * 4;
     static constexpr int kOffDesc = (kOffL + CW * kGP * 4 + 15) / 16 * 16;
     static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
-    static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 2) * 8;  // + epilogue full/empty
+    // + epilogue full/empty + query rotation (fused step)
+    static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 3) * 8;
     static constexpr int kMiscInts = 64;
     static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
     static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * (kRows / 8) * 4;
@@ -214,6 +218,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     const uint32_t bar_empty = bar_full + NSTAGE * 8;       // NSTAGE x 8 bytes
     const uint32_t bar_epi_full = bar_empty + NSTAGE * 8;   // consumers -> epilogue
     const uint32_t bar_epi_empty = bar_epi_full + 8;        // epilogue -> consumers
+    const uint32_t bar_qrot = bar_epi_empty + 8;            // consumers: query rotated
     StageDesc* sEpi = reinterpret_cast<StageDesc*>(smem + L::kOffEpi);
     float* sW = reinterpret_cast<float*>(smem + L::kOffW);
     float* sHM = sW + CW * GP;
@@ -240,6 +245,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         }
         mbar_init(bar_epi_full, CW * 32);
         mbar_init(bar_epi_empty, 32);
+        mbar_init(bar_qrot, CW * 32);
         fence_mbar_init();
         fence_proxy_async_smem();
     }
@@ -412,6 +418,12 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     if (warp == CW) {
         // ===================================================== producer warp
         const uint64_t pol = l2_policy_evict_first();
+        const bool fused = p.cos_sin != nullptr;
+        const T* cos_sin = reinterpret_cast<const T*>(p.cos_sin);
+        T* key_new = reinterpret_cast<T*>(p.key_new);
+        const T* value_new = reinterpret_cast<const T*>(p.value_new);
+        T* kc_new = reinterpret_cast<T*>(p.key_cache);
+        T* vc_new = reinterpret_cast<T*>(p.value_cache);
         const T* query = reinterpret_cast<const T*>(p.query);
         Job* sJob = reinterpret_cast<Job*>(smem + L::kOffProd + kSeqCache * 8);
         const uint32_t sBid = sbase + L::kOffProd + kSeqCache * 8 + kJobRing * (int)sizeof(Job);
@@ -471,6 +483,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 jb.nblk = min(bps, jb.b_hi - jb.cb);
                 jb.ns = ns;
                 jb.seqlen = max(0, min(len, cap_tokens));
+                jb.pos = len - 1;
                 jb.pre = pre;
                 jb.item = item;
                 jb.first = first ? 1 : 0;
@@ -595,6 +608,49 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             for (int b = 0; b < kBpsMax; ++b) ys[b] = __shfl_sync(0xffffffffu, my_y, b);
             return __ballot_sync(0xffffffffu, valid);
         };
+        // Fused decode step: the new token's position, its cos/sin row, and the
+        // write of that token's rotated key and value into the caches.
+        auto pos_ok = [&](const Job& job) -> bool {
+            return job.pos >= 0 && (long long)job.pos < p.cache_rows;
+        };
+        // Called by the whole warp before the copies of the last stage of a
+        // (sequence, kv head) - the stage holding the sequence's last block,
+        // the only one (hence the only CTA) that reads the new token's row:
+        // rotate the key of (s, h) back into the key tensor and, when its
+        // block is mapped, store it and the value into the caches at that
+        // row, then order the stores before the copies.
+        auto write_new_token = [&](const Job& job, int k) {
+            if (job.st_hi != job.ns || job.cb + job.nblk != job.b_hi) return;  // not the last
+            const int blk_i = job.pos / bs;  // block index of the new token
+            const bool in_stage = job.pos < cap_tokens && blk_i >= job.cb &&
+                                  blk_i < job.cb + job.nblk;
+            const int bid = in_stage ? sBidPtr[(k % kJobRing) * kBpsMax + (blk_i - job.cb)] : -1;
+            const bool store = bid >= 0 && (long long)bid < p.num_blocks;
+            const long long row =
+                store ? (((long long)bid * KVH + job.h) * bs + job.pos % bs) * D : 0ll;
+            T* kn = key_new + job.s * p.key_stride + (long long)job.h * D;
+            const T* vn = value_new + job.s * p.value_stride + (long long)job.h * D;
+            const bool rot = pos_ok(job);
+            const T* cs = cos_sin + (rot ? (long long)job.pos * D : 0ll);
+            constexpr int half = D / 2;
+            for (int i = lane; i < half; i += 32) {
+                const float x = Elem<T>::to_f(kn[i]), y = Elem<T>::to_f(kn[i + half]);
+                float xo = x, yo = y;
+                if (rot) rope_pair(x, y, Elem<T>::to_f(cs[i]), Elem<T>::to_f(cs[half + i]), xo, yo);
+                const T xt = Elem<T>::from_f(xo), yt = Elem<T>::from_f(yo);
+                if (store) {
+                    kc_new[row + i] = xt;
+                    kc_new[row + i + half] = yt;
+                }
+                kn[i] = xt;
+                kn[i + half] = yt;
+            }
+            if (store)
+                for (int i = lane; i < D; i += 32) vc_new[row + i] = vn[i];
+            fence_proxy_async_global();
+            __syncwarp();
+        };
+
         // Descriptor and transaction count of a stage (elected lane).
         auto arm_stage = [&](const Job& job, int stage, unsigned vmask) {
             const bool piece_start = job.cb == job.b_lo;
@@ -618,13 +674,15 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 }
             }
             const int flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
-                              (job.nsplits == 1 ? kPieceComplete : 0);
+                              (job.nsplits == 1 ? kPieceComplete : 0) |
+                              (fused && !pos_ok(job) ? kRopeSkip : 0);
+            if (fused && piece_start && !pos_ok(job)) flag_status(TLB_STATUS_BAD_POSITION);
             int4* dw = reinterpret_cast<int4*>(&sDesc[stage]);
             dw[0] = make_int4((int)rows[0], (int)rows[1], (int)rows[2], (int)rows[3]);
             dw[1] = make_int4(flags, job.s, job.h, 2 * job.item + (job.first ? 0 : 1));
             dw[2] = make_int4(job.nsplits, job.jfirst, job.first_slot1, job.s * KVH + job.h);
             const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
-                                   (piece_start ? (uint32_t)(G * D * 2) : 0u);
+                                   (piece_start ? (uint32_t)(G * D * 2 + (fused ? D * 2 : 0)) : 0u);
             mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
         };
         // The copies of the blocks in `mask` (one (block, kv head) tile per
@@ -644,6 +702,10 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             if (with_query) {
                 const T* qsrc = query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
                 bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2), fb);
+                if (fused)  // the cos/sin row of the new token (row 0 when out of the table)
+                    bulk_load(sbase + L::kOffQ + stage * L::kQBytes + GP * D * 2,
+                              cos_sin + (pos_ok(job) ? (long long)job.pos * D : 0ll),
+                              (uint32_t)(D * 2), fb);
             }
         };
         int nf = 0;  // jobs generated (cp.async groups committed)
@@ -675,7 +737,9 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             }
             int32_t ys[kBpsMax];
             const unsigned vmask = stage_blocks(job, k, ys);
+            if (fused) write_new_token(job, k);
             if (elect_one()) {
+                if (fused) fence_proxy_async_global();
                 arm_stage(job, stage, vmask);
                 issue_copies(job, stage, vmask, ys, job.cb == job.b_lo);
             }
@@ -952,6 +1016,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     int stage = 0;
     uint32_t phase = 0;
     uint32_t ephase = 0;
+    uint32_t qphase = 0;
+    const bool fused_q = p.cos_sin != nullptr;
     while (true) {
         bool got = true;
         got = mbar_wait_bounded(bar_full + 8 * stage, phase);
@@ -964,6 +1030,27 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
 
         if (d.flags & kPieceStart) {
             const T* sq = reinterpret_cast<const T*>(smem + L::kOffQ + stage * L::kQBytes);
+            if (fused_q && !(d.flags & kRopeSkip)) {
+                // Fused decode step: rotate the raw query group in place, all
+                // consumer warps sharing the pairs, with the cos/sin row that
+                // came with it; then every warp reads it.
+                T* sqw = reinterpret_cast<T*>(smem + L::kOffQ + stage * L::kQBytes);
+                const T* cs = sq + GP * D;
+                constexpr int half = D / 2;
+                for (int idx = warp * 32 + lane; idx < G * half; idx += CW * 32) {
+                    const int row = idx / half, i = idx - row * half;
+                    float xo, yo;
+                    rope_pair(Elem<T>::to_f(sqw[row * D + i]), Elem<T>::to_f(sqw[row * D + i + half]),
+                              Elem<T>::to_f(cs[i]), Elem<T>::to_f(cs[half + i]), xo, yo);
+                    sqw[row * D + i] = Elem<T>::from_f(xo);
+                    sqw[row * D + i + half] = Elem<T>::from_f(yo);
+                }
+                fence_proxy_async_smem();  // before a later bulk copy into this slot
+                mbar_arrive(bar_qrot);
+                if (!mbar_wait_bounded(bar_qrot, qphase) && lane == 0)
+                    flag_status(TLB_STATUS_WAIT_TIMEOUT);
+                qphase ^= 1;
+            }
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 const int c0 = ks * 16 + 2 * q4;

@@ -108,10 +108,7 @@ __device__ __forceinline__ void rotate(const T* src, T* dst, const T* cs, int ha
     VecIO<T, VEC>::load(src + i0 + half, y);
     float xo[VEC], yo[VEC];
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) {
-        xo[k] = x[k] * c[k] - y[k] * s[k];
-        yo[k] = y[k] * c[k] + x[k] * s[k];
-    }
+    for (int k = 0; k < VEC; ++k) rope_pair(x[k], y[k], c[k], s[k], xo[k], yo[k]);
     VecIO<T, VEC>::store(dst + i0, xo);
     VecIO<T, VEC>::store(dst + i0 + half, yo);
     if (also != nullptr) {
