@@ -249,7 +249,9 @@ int attention_impl(void* out, const void* query, const void* key_cache,
     const bool tc = tlb::attn::tc_supported(dtype, (int)head_dim, group, (int)block_size) &&
                     aligned(query, 16) && aligned(key_cache, 16) && aligned(value_cache, 16) &&
                     rows < (1ull << 31);
-    if (fr != nullptr && !(tc && aligned(fr->cos_sin, 16)))
+    if (fr != nullptr && !(tc && aligned(fr->cos_sin, 16) && aligned(fr->key, 16) &&
+                           aligned(fr->value, 16) && fr->key_stride % 8 == 0 &&
+                           fr->value_stride % 8 == 0))
         return fail(TLB_ERR_UNSUPPORTED,
                     "the fused decode step needs the tensor-core path (fp16/bf16, head_dim 64 "
                     "or 128, group <= 16, block_size 8..64, 16-byte aligned tensors)");

@@ -109,12 +109,37 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 
 // NeoX rotation of the pair (x, y) = (v[i], v[i + rot/2]) by (c, s) =
 // (cos_sin[pos, i], cos_sin[pos, rot/2 + i]) in fp32
-// (pos_encoding_kernel.cu:24-65). Every kernel that rotates goes through this
-// one expression, so they all round to the same bits.
+// (pos_encoding_kernel.cu:24-65). Each product and the sum are rounded on
+// their own (no fused multiply-add contraction): every kernel that rotates,
+// in whatever code it is inlined into, rounds to the same bits, and those are
+// the bits of the same fp32 expression evaluated step by step on the host.
 __device__ __forceinline__ void rope_pair(float x, float y, float c, float s, float& xo,
                                           float& yo) {
-    xo = x * c - y * s;
-    yo = y * c + x * s;
+    xo = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+    yo = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, s));
+}
+
+// Packed pair of 16-bit values (low half first) -> two floats.
+template <typename T> __device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi) {
+    T v[2];
+    memcpy(v, &w, 4);
+    lo = Elem<T>::to_f(v[0]);
+    hi = Elem<T>::to_f(v[1]);
+}
+
+// rope_pair on the two packed columns of x (first half) and of y (the same
+// columns + rot/2), with their packed cos and sin.
+template <typename T>
+__device__ __forceinline__ void rope_packed2(uint32_t& x, uint32_t& y, uint32_t c, uint32_t s) {
+    float x0, x1, y0, y1, c0, c1, s0, s1, xo0, xo1, yo0, yo1;
+    unpack2<T>(x, x0, x1);
+    unpack2<T>(y, y0, y1);
+    unpack2<T>(c, c0, c1);
+    unpack2<T>(s, s0, s1);
+    rope_pair(x0, y0, c0, s0, xo0, yo0);
+    rope_pair(x1, y1, c1, s1, xo1, yo1);
+    x = pack2<T>(xo0, xo1);
+    y = pack2<T>(yo0, yo1);
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)

@@ -48,9 +48,10 @@ enum : int {
     kPieceComplete = 4,
     kTerminate = 8,
     kRopeSkip = 16,  // fused step: the position is outside the cos/sin table, no rotation
+    kNewToken = 32,  // fused step: the stage carries the new token's rows (new_r, new_row)
 };
 
-// Written by the producer as three 16-byte stores.
+// Written by the producer as four 16-byte stores.
 struct alignas(16) StageDesc {
     unsigned rows[4];  // bit r of word r / 32: stage row r holds a token of the piece
     int flags;
@@ -61,6 +62,10 @@ struct alignas(16) StageDesc {
     int jfirst;      // first CTA holding a piece of it
     int first_slot1; // that CTA stored its piece in its second slot
     int u;           // sequence * num_kv_heads + kv head
+    int new_r;       // (kNewToken) stage row of the new token, -1 when not in the stage
+    int new_row;     // (kNewToken) its cache row ((block * kv heads + kv head) * bs + offset),
+                     // -1 when its block is not mapped
+    int pad[2];
 };
 
 constexpr int kSeqCache = 1024; // context lengths kept in shared memory (first 1024 seqs)
@@ -124,8 +129,9 @@ struct TcLayout {
     static constexpr int kRows = CW * kTileRows * kTpw;  // tokens per stage
     static constexpr int kChunks = D / 64;            // 128-byte column chunks per row
     static constexpr int kStageKV = kRows * D * 2;  // bytes of K (or V) per stage
-    // query group of the piece, then (fused RoPE) the cos/sin row of its position
-    static constexpr int kQBytes = 8 * NT * D * 2 + D * 2;
+    // query group of the piece, then (fused decode step) the cos/sin row of
+    // the new token's position and that token's raw key and value rows
+    static constexpr int kQBytes = 8 * NT * D * 2 + 3 * D * 2;
     static constexpr int kGP = 8 * NT;                 // padded heads per piece
     static constexpr int kOFloats = CW * kGP * D;
     static constexpr int kOffK = 0;
@@ -136,13 +142,13 @@ struct TcLayout {
     static constexpr int kOffL = kOffM + CW * kGP * 4;
     static constexpr int kOffDesc = (kOffL + CW * kGP * 4 + 15) / 16 * 16;
     static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
-    // + epilogue full/empty + query rotation (fused step)
-    static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 3) * 8;
+    // + epilogue full/empty
+    static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 2) * 8;
     static constexpr int kMiscInts = 64;
     static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
     static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * (kRows / 8) * 4;
     static constexpr int kOffEpi = (kOffProd + kProdBytes + 15) / 16 * 16;  // hand-off descriptor
-    static constexpr int kOffW = kOffEpi + 64;                         // merge weights, M, L
+    static constexpr int kOffW = kOffEpi + (int)sizeof(StageDesc);     // merge weights, M, L
     static constexpr int kOffCW = kOffW + (CW * kGP + 2 * kGP) * 4;
     static constexpr int kOffOwn = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
     static constexpr int kOffItem = kOffOwn + kGP * D * 4;  // a merging piece's own partial
@@ -218,7 +224,6 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     const uint32_t bar_empty = bar_full + NSTAGE * 8;       // NSTAGE x 8 bytes
     const uint32_t bar_epi_full = bar_empty + NSTAGE * 8;   // consumers -> epilogue
     const uint32_t bar_epi_empty = bar_epi_full + 8;        // epilogue -> consumers
-    const uint32_t bar_qrot = bar_epi_empty + 8;            // consumers: query rotated
     StageDesc* sEpi = reinterpret_cast<StageDesc*>(smem + L::kOffEpi);
     float* sW = reinterpret_cast<float*>(smem + L::kOffW);
     float* sHM = sW + CW * GP;
@@ -245,7 +250,6 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         }
         mbar_init(bar_epi_full, CW * 32);
         mbar_init(bar_epi_empty, 32);
-        mbar_init(bar_qrot, CW * 32);
         fence_mbar_init();
         fence_proxy_async_smem();
     }
@@ -420,10 +424,24 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         const uint64_t pol = l2_policy_evict_first();
         const bool fused = p.cos_sin != nullptr;
         const T* cos_sin = reinterpret_cast<const T*>(p.cos_sin);
-        T* key_new = reinterpret_cast<T*>(p.key_new);
+        const T* key_new = reinterpret_cast<const T*>(p.key_new);
         const T* value_new = reinterpret_cast<const T*>(p.value_new);
-        T* kc_new = reinterpret_cast<T*>(p.key_cache);
-        T* vc_new = reinterpret_cast<T*>(p.value_cache);
+        // Fused decode step: the new token (position job.pos) has a cos/sin row.
+        auto pos_ok = [&](const Job& job) -> bool {
+            return job.pos >= 0 && (long long)job.pos < p.cache_rows;
+        };
+        // Whether this job is the last stage of a piece that runs to its
+        // (sequence, kv head)'s end: that stage alone holds the sequence's
+        // last block, so it carries the new token's rows.
+        auto carries_new_token = [&](const Job& job) -> bool {
+            return fused && job.st_hi == job.ns && job.cb + job.nblk == job.b_hi;
+        };
+        // Whether the new token's block is among this stage's blocks.
+        auto new_token_here = [&](const Job& job) -> bool {
+            const int blk_i = job.pos / bs;
+            return job.pos >= 0 && job.pos < cap_tokens && blk_i >= job.cb &&
+                   blk_i < job.cb + job.nblk;
+        };
         const T* query = reinterpret_cast<const T*>(p.query);
         Job* sJob = reinterpret_cast<Job*>(smem + L::kOffProd + kSeqCache * 8);
         const uint32_t sBid = sbase + L::kOffProd + kSeqCache * 8 + kJobRing * (int)sizeof(Job);
@@ -575,9 +593,16 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             // The query group of a new piece is pulled into L2 (and its page
             // into the TLB) kPrefetch stages before its bulk load. L2 is the
             // coherence point, so this is safe before griddepcontrol.wait.
-            if (lane == 0 && pj.valid && pj.cb == pj.b_lo)
+            if (lane == 0 && pj.valid && pj.cb == pj.b_lo) {
                 bulk_prefetch_l2(query + ((long long)pj.s * p.num_heads + (long long)pj.h * G) * D,
                                  (uint32_t)(G * D * 2));
+            }
+            if (lane == 0 && pj.valid && carries_new_token(pj)) {  // its raw key and value
+                bulk_prefetch_l2(key_new + pj.s * p.key_stride + (long long)pj.h * D,
+                                 (uint32_t)(D * 2));
+                bulk_prefetch_l2(value_new + pj.s * p.value_stride + (long long)pj.h * D,
+                                 (uint32_t)(D * 2));
+            }
             if (pj.valid && lane < pj.nblk)
                 cp_async_4(sBid + (uint32_t)(slot * kBpsMax + lane) * 4u,
                            p.block_tables + (long long)pj.s * p.max_blocks + pj.cb + lane);
@@ -608,51 +633,9 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             for (int b = 0; b < kBpsMax; ++b) ys[b] = __shfl_sync(0xffffffffu, my_y, b);
             return __ballot_sync(0xffffffffu, valid);
         };
-        // Fused decode step: the new token's position, its cos/sin row, and the
-        // write of that token's rotated key and value into the caches.
-        auto pos_ok = [&](const Job& job) -> bool {
-            return job.pos >= 0 && (long long)job.pos < p.cache_rows;
-        };
-        // Called by the whole warp before the copies of the last stage of a
-        // (sequence, kv head) - the stage holding the sequence's last block,
-        // the only one (hence the only CTA) that reads the new token's row:
-        // rotate the key of (s, h) back into the key tensor and, when its
-        // block is mapped, store it and the value into the caches at that
-        // row, then order the stores before the copies.
-        auto write_new_token = [&](const Job& job, int k) {
-            if (job.st_hi != job.ns || job.cb + job.nblk != job.b_hi) return;  // not the last
-            const int blk_i = job.pos / bs;  // block index of the new token
-            const bool in_stage = job.pos < cap_tokens && blk_i >= job.cb &&
-                                  blk_i < job.cb + job.nblk;
-            const int bid = in_stage ? sBidPtr[(k % kJobRing) * kBpsMax + (blk_i - job.cb)] : -1;
-            const bool store = bid >= 0 && (long long)bid < p.num_blocks;
-            const long long row =
-                store ? (((long long)bid * KVH + job.h) * bs + job.pos % bs) * D : 0ll;
-            T* kn = key_new + job.s * p.key_stride + (long long)job.h * D;
-            const T* vn = value_new + job.s * p.value_stride + (long long)job.h * D;
-            const bool rot = pos_ok(job);
-            const T* cs = cos_sin + (rot ? (long long)job.pos * D : 0ll);
-            constexpr int half = D / 2;
-            for (int i = lane; i < half; i += 32) {
-                const float x = Elem<T>::to_f(kn[i]), y = Elem<T>::to_f(kn[i + half]);
-                float xo = x, yo = y;
-                if (rot) rope_pair(x, y, Elem<T>::to_f(cs[i]), Elem<T>::to_f(cs[half + i]), xo, yo);
-                const T xt = Elem<T>::from_f(xo), yt = Elem<T>::from_f(yo);
-                if (store) {
-                    kc_new[row + i] = xt;
-                    kc_new[row + i + half] = yt;
-                }
-                kn[i] = xt;
-                kn[i + half] = yt;
-            }
-            if (store)
-                for (int i = lane; i < D; i += 32) vc_new[row + i] = vn[i];
-            fence_proxy_async_global();
-            __syncwarp();
-        };
-
         // Descriptor and transaction count of a stage (elected lane).
-        auto arm_stage = [&](const Job& job, int stage, unsigned vmask) {
+        auto arm_stage = [&](const Job& job, int stage, unsigned vmask, bool new_tok, int new_r,
+                             int new_row) {
             const bool piece_start = job.cb == job.b_lo;
             const bool piece_end = job.cb + job.nblk == job.b_hi;
             // Valid rows: inside the stage, before the context end, in a
@@ -675,20 +658,25 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             }
             const int flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
                               (job.nsplits == 1 ? kPieceComplete : 0) |
-                              (fused && !pos_ok(job) ? kRopeSkip : 0);
+                              (fused && !pos_ok(job) ? kRopeSkip : 0) | (new_tok ? kNewToken : 0);
             if (fused && piece_start && !pos_ok(job)) flag_status(TLB_STATUS_BAD_POSITION);
             int4* dw = reinterpret_cast<int4*>(&sDesc[stage]);
             dw[0] = make_int4((int)rows[0], (int)rows[1], (int)rows[2], (int)rows[3]);
             dw[1] = make_int4(flags, job.s, job.h, 2 * job.item + (job.first ? 0 : 1));
             dw[2] = make_int4(job.nsplits, job.jfirst, job.first_slot1, job.s * KVH + job.h);
+            dw[3] = make_int4(new_r, new_row, 0, 0);
+            // KV tiles, the query group and cos/sin row of a piece start, the
+            // new token's key and value rows (and cos/sin row) of its stage
             const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
-                                   (piece_start ? (uint32_t)(G * D * 2 + (fused ? D * 2 : 0)) : 0u);
+                                   (piece_start ? (uint32_t)(G * D * 2 + (fused ? D * 2 : 0)) : 0u) +
+                                   (new_tok ? (uint32_t)(2 * D * 2 + (piece_start ? 0 : D * 2)) : 0u);
             mbar_arrive_expect_tx(bar_full + 8 * stage, bytes);
         };
         // The copies of the blocks in `mask` (one (block, kv head) tile per
-        // copy: [chunk][bs rows][128 B]) and, if asked, of the query group.
+        // copy: [chunk][bs rows][128 B]) and, if asked, of the query group
+        // and of the new token's rows.
         auto issue_copies = [&](const Job& job, int stage, unsigned mask,
-                                const int32_t (&ys)[kBpsMax], bool with_query) {
+                                const int32_t (&ys)[kBpsMax], bool with_query, bool new_tok) {
             const uint32_t fb = bar_full + 8 * stage;
             const uint32_t kdst = sbase + L::kOffK + stage * L::kStageKV;
             const uint32_t vdst = sbase + L::kOffV + stage * L::kStageKV;
@@ -702,10 +690,16 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             if (with_query) {
                 const T* qsrc = query + ((long long)job.s * p.num_heads + (long long)job.h * G) * D;
                 bulk_load(sbase + L::kOffQ + stage * L::kQBytes, qsrc, (uint32_t)(G * D * 2), fb);
-                if (fused)  // the cos/sin row of the new token (row 0 when out of the table)
-                    bulk_load(sbase + L::kOffQ + stage * L::kQBytes + GP * D * 2,
-                              cos_sin + (pos_ok(job) ? (long long)job.pos * D : 0ll),
-                              (uint32_t)(D * 2), fb);
+            }
+            const uint32_t cdst = sbase + L::kOffQ + stage * L::kQBytes + GP * D * 2;
+            if (fused && (with_query || new_tok))  // cos/sin row of the new token (row 0 when out of the table)
+                bulk_load(cdst, cos_sin + (pos_ok(job) ? (long long)job.pos * D : 0ll),
+                          (uint32_t)(D * 2), fb);
+            if (new_tok) {
+                bulk_load(cdst + D * 2, key_new + job.s * p.key_stride + (long long)job.h * D,
+                          (uint32_t)(D * 2), fb);
+                bulk_load(cdst + 2 * D * 2, value_new + job.s * p.value_stride + (long long)job.h * D,
+                          (uint32_t)(D * 2), fb);
             }
         };
         int nf = 0;  // jobs generated (cp.async groups committed)
@@ -737,11 +731,21 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             }
             int32_t ys[kBpsMax];
             const unsigned vmask = stage_blocks(job, k, ys);
-            if (fused) write_new_token(job, k);
+            // Fused decode step: where the new token sits in this stage and in
+            // the cache (the consumers write its rows; see below).
+            const bool new_tok = carries_new_token(job);
+            int new_r = -1, new_row = -1;
+            if (new_tok && new_token_here(job)) {
+                const int b = job.pos / bs - job.cb;
+                new_r = job.pos - job.cb * bs;
+                int32_t y = 0;
+#pragma unroll
+                for (int bb = 0; bb < kBpsMax; ++bb) y = bb == b ? ys[bb] : y;
+                if ((vmask >> b) & 1u) new_row = y + job.pos % bs;
+            }
             if (elect_one()) {
-                if (fused) fence_proxy_async_global();
-                arm_stage(job, stage, vmask);
-                issue_copies(job, stage, vmask, ys, job.cb == job.b_lo);
+                arm_stage(job, stage, vmask, new_tok, new_r, new_row);
+                issue_copies(job, stage, vmask, ys, job.cb == job.b_lo, new_tok);
             }
             __syncwarp();
             if (++stage == NSTAGE) { stage = 0; phase ^= 1; }
@@ -1016,8 +1020,65 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     int stage = 0;
     uint32_t phase = 0;
     uint32_t ephase = 0;
-    uint32_t qphase = 0;
     const bool fused_q = p.cos_sin != nullptr;
+    T* key_new = reinterpret_cast<T*>(p.key_new);
+    T* kc_new = reinterpret_cast<T*>(p.key_cache);
+    T* vc_new = reinterpret_cast<T*>(p.value_cache);
+    // Fused decode step. The stage that holds a sequence's last block (the
+    // last of the piece that runs to the end of its (sequence, kv head))
+    // brought the new token's raw key and value rows and its cos/sin row into
+    // the stage's query slot. One warp (the one whose tile holds the token, or
+    // warp 0 when the token is in no stage) rotates the key, writes it back
+    // into the key tensor and, when the token's block is mapped, into both
+    // caches and over the token's row of the stage, where the copy of the
+    // block brought the row as it was before this step. Nothing else reads
+    // that cache row during the launch, so the global stores need no ordering.
+    auto write_new_token = [&](int stg, const StageDesc& dd) {
+        constexpr int kU = D / 8;    // 16-byte units of a row
+        constexpr int kHU = kU / 2;  // units of its first half
+        const uint8_t* slot = smem + L::kOffQ + stg * L::kQBytes + GP * D * 2;
+        const uint4* cs = reinterpret_cast<const uint4*>(slot);
+        const uint4* kraw = reinterpret_cast<const uint4*>(slot + D * 2);
+        const uint4* vraw = reinterpret_cast<const uint4*>(slot + 2 * D * 2);
+        const bool store = dd.new_row >= 0;  // implies new_r >= 0
+        const long long grow = (long long)dd.new_row * D;
+        // the token's row in the stage: block tile new_r / bs, row rr, with
+        // the 128-byte swizzle of the copies on its 16-byte units
+        const int rr = store ? dd.new_r % bs : 0;
+        const int roff = store ? (dd.new_r / bs) * (bs * D * 2) + rr * 128 : 0;
+        auto unit_off = [&](int u) -> int {
+            return roff + (u >> 3) * (int)chunk_bytes + (((u & 7) ^ (rr & 7)) << 4);
+        };
+        if (lane < kHU) {
+            uint4 x = kraw[lane], y = kraw[lane + kHU];
+            if (!(dd.flags & kRopeSkip)) {
+                const uint4 c = cs[lane], sn = cs[lane + kHU];
+                rope_packed2<T>(x.x, y.x, c.x, sn.x);
+                rope_packed2<T>(x.y, y.y, c.y, sn.y);
+                rope_packed2<T>(x.z, y.z, c.z, sn.z);
+                rope_packed2<T>(x.w, y.w, c.w, sn.w);
+            }
+            uint4* kn = reinterpret_cast<uint4*>(key_new + (long long)dd.seq * p.key_stride +
+                                                 (long long)dd.kvh * D);
+            kn[lane] = x;
+            kn[lane + kHU] = y;
+            if (store) {
+                uint4* kc = reinterpret_cast<uint4*>(kc_new + grow);
+                kc[lane] = x;
+                kc[lane + kHU] = y;
+                uint8_t* kst = smem + L::kOffK + stg * L::kStageKV;
+                *reinterpret_cast<uint4*>(kst + unit_off(lane)) = x;
+                *reinterpret_cast<uint4*>(kst + unit_off(lane + kHU)) = y;
+            }
+        } else if (lane >= 16 && lane < 16 + kU && store) {
+            const int u = lane - 16;
+            const uint4 v = vraw[u];
+            reinterpret_cast<uint4*>(vc_new + grow)[u] = v;
+            *reinterpret_cast<uint4*>(smem + L::kOffV + stg * L::kStageKV + unit_off(u)) = v;
+        }
+        fence_proxy_async_smem();  // before the stage's next copy overwrites these rows
+        __syncwarp();
+    };
     while (true) {
         bool got = true;
         got = mbar_wait_bounded(bar_full + 8 * stage, phase);
@@ -1030,27 +1091,6 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
 
         if (d.flags & kPieceStart) {
             const T* sq = reinterpret_cast<const T*>(smem + L::kOffQ + stage * L::kQBytes);
-            if (fused_q && !(d.flags & kRopeSkip)) {
-                // Fused decode step: rotate the raw query group in place, all
-                // consumer warps sharing the pairs, with the cos/sin row that
-                // came with it; then every warp reads it.
-                T* sqw = reinterpret_cast<T*>(smem + L::kOffQ + stage * L::kQBytes);
-                const T* cs = sq + GP * D;
-                constexpr int half = D / 2;
-                for (int idx = warp * 32 + lane; idx < G * half; idx += CW * 32) {
-                    const int row = idx / half, i = idx - row * half;
-                    float xo, yo;
-                    rope_pair(Elem<T>::to_f(sqw[row * D + i]), Elem<T>::to_f(sqw[row * D + i + half]),
-                              Elem<T>::to_f(cs[i]), Elem<T>::to_f(cs[half + i]), xo, yo);
-                    sqw[row * D + i] = Elem<T>::from_f(xo);
-                    sqw[row * D + i + half] = Elem<T>::from_f(yo);
-                }
-                fence_proxy_async_smem();  // before a later bulk copy into this slot
-                mbar_arrive(bar_qrot);
-                if (!mbar_wait_bounded(bar_qrot, qphase) && lane == 0)
-                    flag_status(TLB_STATUS_WAIT_TIMEOUT);
-                qphase ^= 1;
-            }
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 const int c0 = ks * 16 + 2 * q4;
@@ -1059,6 +1099,22 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 qa[ks][2] = g < G ? *reinterpret_cast<const uint32_t*>(sq + g * D + c0 + 8) : 0u;
                 qa[ks][3] =
                     g + 8 < G ? *reinterpret_cast<const uint32_t*>(sq + (g + 8) * D + c0 + 8) : 0u;
+            }
+            if (fused_q && !(d.flags & kRopeSkip)) {
+                // Fused decode step: rotate the raw query group in registers
+                // with the cos/sin row that came with it. Columns c and
+                // c + D/2 of a fragment word sit in k-steps ks and ks + KS/2
+                // of the same lane, so each lane rotates its own pairs.
+                const T* cs = sq + GP * D;
+#pragma unroll
+                for (int ks = 0; ks < KS / 2; ++ks)
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int col = ks * 16 + 2 * q4 + (r >= 2 ? 8 : 0);
+                        rope_packed2<T>(qa[ks][r], qa[ks + KS / 2][r],
+                                        *reinterpret_cast<const uint32_t*>(cs + col),
+                                        *reinterpret_cast<const uint32_t*>(cs + D / 2 + col));
+                    }
             }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
@@ -1074,6 +1130,9 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         for (int t = 0; t < TPW; ++t) {
         const int r0 = (t * CW + warp) * kTileRows;
         const uint32_t ld_off = ld_off_t[t];
+        if ((d.flags & kNewToken) &&
+            (d.new_r >= 0 ? d.new_r / kTileRows == t * CW + warp : (t == 0 && warp == 0)))
+            write_new_token(stage, d);
         // Valid rows of this 16-token tile.
         const unsigned vmask = (sDesc[stage].rows[r0 >> 5] >> (r0 & 31)) & 0xffffu;
 
