@@ -202,7 +202,8 @@ TLB_API int tlb_paged_attention_with_rope(void* out, const void* query, void* ke
  *   cos_sin_cache : [cache_rows, rot_dim]; cos in [:rot_dim/2], sin after
  *
  * Pairs (i, i + rot_dim/2), i < rot_dim/2, of each head are rotated:
- * x' = x cos - y sin, y' = y cos + x sin, in fp32, rounded once to dtype.
+ * x' = x cos - y sin, y' = y cos + x sin, in fp32 with each product and
+ * the sum rounded on its own (no multiply-add), then rounded once to dtype.
  * Query elements at and beyond rot_dim are copied to `out` unchanged.
  * ---------------------------------------------------------------------- */
 TLB_API int tlb_rotary_embedding_neox(void* out, const void* positions, int pos_dtype,

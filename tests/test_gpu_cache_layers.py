@@ -7,7 +7,7 @@ import torch
 from conftest import GOLDEN
 from cscr import _lib
 from cscr import cache as C
-from helpers import check_attention, tol_for
+from helpers import check_attention
 from oracle import decode_oracle as O
 from paged_decode import metadata as M
 from paged_decode import workloads as W
@@ -72,8 +72,10 @@ def test_decode_metadata_matches_reference_worker(built_lib):
 
 
 @pytest.mark.parametrize("build", [torch.float32, torch.bfloat16])
-def test_paged_attention_with_rope_layer(build, built_lib):
-    """Reference layer forward: RoPE -> _write_kv_cache -> attention, on the fused ops."""
+@pytest.mark.parametrize("given_positions", [True, False], ids=["positions", "one_launch"])
+def test_paged_attention_with_rope_layer(build, given_positions, built_lib):
+    """Reference layer forward: RoPE -> _write_kv_cache -> attention, on the fused ops;
+    with positions=None (decode positions seq_lens - 1) as one launch."""
     spec = W.DecodeSpec("layer", [1, 17, 64, 300, 2048, 4096, 33, 1000], 16, 2, 128, 16,
                         "bfloat16", num_blocks=2048, rope_theta=1e6, max_position=4096)
     b = W.make_batch(spec)
@@ -92,12 +94,12 @@ def test_paged_attention_with_rope_layer(build, built_lib):
     q_rot, k_rot = O.rotary_embedding_neox(W.to_numpy(b.positions), q_np, k_np, 128,
                                            W.to_numpy(cs), "bfloat16")
     kc, vc = W.to_numpy(b.key_cache), W.to_numpy(b.value_cache)
-    out = layer(b.positions, b.query, b.key, b.value, b.key_cache, b.value_cache,
-                b.block_tables, b.seq_lens)
-    # the layer rotated `key` in place (as the reference does) ...
+    assert torch.equal(b.positions.to(torch.int64), b.seq_lens.to(torch.int64) - 1)
+    out = layer(b.positions if given_positions else None, b.query, b.key, b.value,
+                b.key_cache, b.value_cache, b.block_tables, b.seq_lens)
+    # the layer rotated `key` in place (as the reference does), to the oracle's bits ...
     k_dev = W.to_numpy(b.key.reshape(S, -1))
-    np.testing.assert_allclose(O.to_f32(k_dev, "bfloat16"), O.to_f32(k_rot, "bfloat16"),
-                               **tol_for("bfloat16"))
+    assert np.array_equal(k_dev, k_rot)
     # ... and wrote exactly that key and the value where _write_kv_cache would
     O.write_kv_cache(k_dev, W.to_numpy(b.value), W.to_numpy(b.positions), kc, vc,
                      W.to_numpy(b.block_tables))

@@ -4,8 +4,9 @@ the same step as separate launches, and through them against the oracle.
 The separate launches are rotary_embedding_neox_with_cache (positions
 seq_lens - 1, block-table addressing) followed by paged_attention; both are
 checked against the oracle elsewhere. Here: the cache rows and the rotated key
-the fused launch leaves must be the same bits, the attention output must
-agree within the attention tolerance, and edge cases (negative block ids,
+the fused launch leaves must be the same bits, and so must the attention
+output (the query is rotated by the same function, the caches hold the same
+rows, and the work partition and merge order are the same), and edge cases (negative block ids,
 positions outside the cos/sin table, empty sequences, many splits) behave as
 the separate launches do.
 """
@@ -72,6 +73,9 @@ def _compare(b, repeats=2):
         assert torch.equal(vc.view(torch.int16), vc_ref.view(torch.int16)), "value cache"
         tol = tol_for(b.spec.dtype)
         torch.testing.assert_close(out.float(), ref.float(), atol=tol["atol"], rtol=tol["rtol"])
+        # same query bits (one rotation function), same cache rows, same work
+        # partition and merge order: the very same output bits
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), "attention output"
     return out, kc, vc, _lib.device_status()
 
 

@@ -10,6 +10,13 @@ block tables exactly as ``_write_kv_cache`` addresses it, then the attention
 kernel. Unlike the reference it does not synchronise the host (the
 ``valid.any()`` of :103) and converts the cos/sin table once per device and
 dtype instead of on every call (:148-150).
+
+``positions=None`` states the decode invariant the reference's worker builds
+(src/worker/worker.py:144-146,154: a decode token sits at position
+``context_len - 1`` and ``seq_lens`` holds the context lengths), so the
+position of every token is ``seq_lens - 1``; with full-width rotary
+(``rotary_dim == head_size``) the whole step then runs as ONE launch
+(``cscr.attention.paged_attention_with_rope``).
 """
 
 from __future__ import annotations
@@ -69,7 +76,7 @@ class PagedAttentionWithRoPE(PagedAttention):
         _Cache.write_kv_cache(key, value, positions, key_cache, value_cache,
                               block_tables.to(torch.int32))
 
-    def forward(self, positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
+    def forward(self, positions: torch.Tensor | None, query: torch.Tensor, key: torch.Tensor,
                 value: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                 block_tables: torch.Tensor, seq_lens: torch.Tensor) -> torch.Tensor:
         if query.dim() != 3:
@@ -85,11 +92,19 @@ class PagedAttentionWithRoPE(PagedAttention):
             raise NotImplementedError(
                 "PagedAttentionWithRoPE only supports decode: there must be one token per sequence")
 
-        query_2d = query.reshape(num_tokens, num_heads * head_size).contiguous()
-        key_2d = key.reshape(num_tokens, -1).contiguous()
         cos_sin_cache = self._table(query.device, query.dtype)
         tables = block_tables if block_tables.dtype == torch.int32 else block_tables.to(torch.int32)
         tables = tables.contiguous()
+        if positions is None:
+            if self.rotary_dim == head_size:
+                # RoPE, cache write and attention in one launch; the key is
+                # rotated in place, as rotary_embedding_neox does to it
+                return _C.paged_attention_with_rope(
+                    query.contiguous(), key, value, key_cache, value_cache, tables, seq_lens,
+                    cos_sin_cache, self.scale)
+            positions = seq_lens.to(torch.int64) - 1
+        query_2d = query.reshape(num_tokens, num_heads * head_size).contiguous()
+        key_2d = key.reshape(num_tokens, -1).contiguous()
         fused = key_cache.dtype == query.dtype and value.dtype == query.dtype
         if fused:
             query_2d = _PE.rotary_embedding_neox_with_cache(
