@@ -5,9 +5,9 @@ context U[128, 4096], 16 query / 2 KV heads, head_dim 128, block_size 16,
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one decode step of one attention layer: the fused RoPE + cache
-write kernel, then the paged-attention kernel, for every sequence of the
-batch. Steps rotate over independent layers (own KV pool, tables, inputs), so
+One step = one decode step of one attention layer, for every sequence of the
+batch: RoPE, the KV-cache write of the new token and paged attention, one
+launch. Steps rotate over independent layers (own KV pool, tables, inputs), so
 consecutive steps never find their KV in L2. With N GPUs (torchrun, one
 process per GPU) the global batch is 64*N sequences drawn from the same
 distribution and assigned to GPUs by LPT on context length; each GPU owns its
@@ -387,9 +387,12 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
     S, H, KVH, D = len(spec0.seq_lens), spec0.num_heads, spec0.num_kv_heads, spec0.head_dim
     maxB = max(b.block_tables.shape[1] for b in layers)
     layout, total = pack_layout(S, H, KVH, D, maxB)
-    hosts, devs, views, outs = [], [], [], []
-    for b in layers:
-        h = torch.zeros(total, dtype=torch.uint8).pin_memory()
+    nl = len(layers)
+    # Host inputs of the nl layers, back to back in one pinned buffer, and two
+    # device staging banks of the same size.
+    host = torch.zeros(nl * total, dtype=torch.uint8).pin_memory()
+    for r, b in enumerate(layers):
+        h = host[r * total:(r + 1) * total]
 
         def put(name, t):
             o, n = layout[name]
@@ -399,55 +402,65 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
         bt[:, : b.block_tables.shape[1]] = b.block_tables.cpu()
         put("query", b.query); put("key", b.key); put("value", b.value)
         put("tables", bt); put("lens", b.seq_lens)
-        d = torch.empty(total, dtype=torch.uint8, device=dev)
+    banks = torch.empty(2, nl * total, dtype=torch.uint8, device=dev)
+
+    def views_of(bank, r):
+        d = banks[bank, r * total:(r + 1) * total]
 
         def view(name, dtype, shape):
             o, n = layout[name]
             return d[o:o + n].view(dtype).view(*shape)
 
-        v = dict(query=view("query", torch.bfloat16, (S, H, D)),
-                 key=view("key", torch.bfloat16, (S, KVH * D)),
-                 value=view("value", torch.bfloat16, (S, KVH, D)),
-                 tables=view("tables", torch.int32, (S, maxB)),
-                 lens=view("lens", torch.int32, (S,)))
-        hosts.append(h); devs.append(d); views.append(v)
-        outs.append(torch.empty(S, H, D, dtype=torch.bfloat16).pin_memory())
+        return dict(query=view("query", torch.bfloat16, (S, H, D)),
+                    key=view("key", torch.bfloat16, (S, KVH * D)),
+                    value=view("value", torch.bfloat16, (S, KVH, D)),
+                    tables=view("tables", torch.int32, (S, maxB)),
+                    lens=view("lens", torch.int32, (S,)))
 
-    nl = len(layers)
-    # A decode loop as a serving engine runs it: the steps' public-API calls
-    # captured once into a CUDA graph, with the copies on their own streams.
-    # Step i's input copy overlaps step i-1's compute and step i-2's read-back;
-    # a layer's device staging buffer is refilled only after the compute that
-    # read it (nl steps earlier) has finished. Every replay moves every step's
-    # inputs host-to-device and its output device-to-host.
+    views = [[views_of(k, r) for r in range(nl)] for k in range(2)]
+    # A decode pass as a serving engine runs it: the public-API calls of a
+    # 36-layer model's pass (Qwen2.5-3B has 36 layers) captured once into a
+    # CUDA graph. The steps go in groups of nl consecutive layers: one pinned
+    # host-to-device copy brings a group's inputs into a staging bank (two
+    # banks, so a group's copy overlaps the previous group's compute), the
+    # group's steps run back to back with programmatic overlap (each kernel
+    # reads only its context lengths and block tables - which the copy, a full
+    # dependency, wrote - before it waits for the kernel ahead of it), and
+    # the group's outputs are read back on their own stream while the next
+    # group computes. Every step's inputs and output cross PCIe every replay.
+    groups = -(-36 // nl)
+    per_graph = groups * nl
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    per_graph = 2 * nl
+    outs = [torch.empty(S, H, D, dtype=torch.bfloat16).pin_memory() for _ in range(per_graph)]
 
     def steps_block():
-        done_comp = [None] * nl
         fork = torch.cuda.Event()
         fork.record(stream)
         s_in.wait_event(fork)
         s_out.wait_event(fork)
-        for i in range(per_graph):
-            r = i % nl
-            b, v = layers[r], views[r]
-            done_in = torch.cuda.Event()
+        done = []
+        for gi in range(groups):
+            bank = gi % 2
+            ready = torch.cuda.Event()
             with torch.cuda.stream(s_in):
-                if done_comp[r] is not None:
-                    s_in.wait_event(done_comp[r])
-                devs[r].copy_(hosts[r], non_blocking=True)
-                done_in.record(s_in)
-            stream.wait_event(done_in)
-            out = A.paged_attention_with_rope(v["query"], v["key"], v["value"], b.key_cache,
-                                              b.value_cache, v["tables"], v["lens"],
-                                              b.cos_sin_cache, b.scale)
+                if gi >= 2:
+                    s_in.wait_event(done[gi - 2])  # the bank's previous readers finished
+                banks[bank].copy_(host, non_blocking=True)
+                ready.record(s_in)
+            stream.wait_event(ready)
+            produced = []
+            for r in range(nl):
+                b, v = layers[r], views[bank][r]
+                produced.append(A.paged_attention_with_rope(
+                    v["query"], v["key"], v["value"], b.key_cache, b.value_cache, v["tables"],
+                    v["lens"], b.cos_sin_cache, b.scale, overlap_prologue=True))
             ev = torch.cuda.Event()
             ev.record(stream)
-            done_comp[r] = ev
+            done.append(ev)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev)
-                outs[r].copy_(out, non_blocking=True)
+                for r, out in enumerate(produced):
+                    outs[gi * nl + r].copy_(out, non_blocking=True)
         join_in, join_out = torch.cuda.Event(), torch.cuda.Event()
         join_in.record(s_in)
         join_out.record(s_out)
@@ -457,6 +470,8 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
     reps = max(1, (args.steps // 4) // per_graph)
     steps = reps * per_graph
     with torch.cuda.stream(stream):
+        banks[0].copy_(host)
+        banks[1].copy_(host)
         steps_block()  # warm: workspaces, tensor maps
         torch.cuda.synchronize(dev)
         g = torch.cuda.CUDAGraph()
@@ -483,10 +498,11 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
     return {"value": round(S * world * steps / (ms / 1e3), 1), "unit": UNIT,
             "h2d_bytes_per_step": int(total), "d2h_bytes_per_step": int(S * H * D * 2),
             "steps": steps,
-            "path": "cscr.attention.paged_attention_with_rope (RoPE + cache write + "
-                    "attention), one pinned H2D + one D2H per step, "
-                    "copies on their own streams overlapping the neighbouring steps' compute, "
-                    f"{per_graph} steps per CUDA-graph replay"}
+            "path": "cscr.attention.paged_attention_with_rope (RoPE + cache write + attention, "
+                    "overlap_prologue=True), per step its inputs host-to-device from pinned memory "
+                    f"(one copy per group of {nl} consecutive steps, double-buffered) and its "
+                    f"output device-to-host, copies on their own streams; {per_graph} steps "
+                    "(a 36-layer decode pass) per CUDA-graph replay"}
 
 
 # ------------------------------------------------------------ CPU side
