@@ -49,6 +49,7 @@ enum : int {
     kTerminate = 8,
     kRopeSkip = 16,  // fused step: the position is outside the cos/sin table, no rotation
     kNewToken = 32,  // fused step: the stage carries the new token's rows (new_r, new_row)
+    kCtaLast = 64,   // the last stage of the CTA's range
 };
 
 // Written by the producer as four 16-byte stores.
@@ -90,7 +91,8 @@ constexpr int kCostPiece = 5;
 // at most two jobs are generated per issued stage, so the lookahead never
 // comes as a burst between two issues.
 constexpr int kPrefetch = TLB_ATTN_PREFETCH;
-static_assert(kPrefetch >= 1 && kPrefetch <= 6, "cp.async group waits handle up to 5 pending");
+static_assert(kPrefetch >= 2 && kPrefetch <= 6,
+              "the job after the one issued is in the ring; cp.async waits handle <= 5 pending");
 #ifndef TLB_ATTN_TAIL_DEN
 #define TLB_ATTN_TAIL_DEN 0
 #endif
@@ -117,6 +119,34 @@ struct alignas(8) Job {
     int pos;         // position of the sequence's new token (its length - 1)
 };
 
+// Merge arithmetic of split pieces, shared by the epilogue warp's merge and
+// the consumer warps' merge of a CTA's last piece: explicit roundings, so
+// either path gives the same bits for the same pieces.
+//
+// Weights of one head over pieces j < cn: w[j * stride] holds piece j's max
+// on entry and its weight exp2(m_j - M) on exit; returns lt + sum_j w_j l_j.
+__device__ __forceinline__ float piece_weights(float* w, const float* l, int cn, int stride,
+                                               float M, float lt) {
+    for (int j = 0; j < cn; ++j) {
+        const float wt = M == -INFINITY ? 0.f : exp2f(w[j * stride] - M);
+        w[j * stride] = wt;
+        lt = __fmaf_rn(wt, l[j * stride], lt);
+    }
+    return lt;
+}
+// a += w0 v0 + w1 v1, elementwise (pieces are summed in pairs, ascending)
+__device__ __forceinline__ void add_pair(float4& a, float w0, const float4& v0, float w1,
+                                         const float4& v1) {
+    a.x = __fadd_rn(a.x, __fmaf_rn(w1, v1.x, __fmul_rn(w0, v0.x)));
+    a.y = __fadd_rn(a.y, __fmaf_rn(w1, v1.y, __fmul_rn(w0, v0.y)));
+    a.z = __fadd_rn(a.z, __fmaf_rn(w1, v1.z, __fmul_rn(w0, v0.z)));
+    a.w = __fadd_rn(a.w, __fmaf_rn(w1, v1.w, __fmul_rn(w0, v0.w)));
+}
+// Most pieces the consumer warps merge themselves (the (m, l) of every piece
+// sit in the hand-off buffer meanwhile); a unit cut into more goes to the
+// epilogue warp.
+constexpr int kConsumerMergeMax = 64;
+
 #ifndef TLB_ATTN_TPW64
 #define TLB_ATTN_TPW64 2
 #endif
@@ -142,8 +172,8 @@ struct TcLayout {
     static constexpr int kOffL = kOffM + CW * kGP * 4;
     static constexpr int kOffDesc = (kOffL + CW * kGP * 4 + 15) / 16 * 16;
     static constexpr int kOffBar = (kOffDesc + NSTAGE * (int)sizeof(StageDesc) + 7) / 8 * 8;
-    // + epilogue full/empty
-    static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 2) * 8;
+    // + epilogue full/empty + consumer warps' own barrier
+    static constexpr int kOffMisc = kOffBar + (2 * NSTAGE + 3) * 8;
     static constexpr int kMiscInts = 64;
     static constexpr int kOffProd = kOffMisc + kMiscInts * 4;  // producer scratch
     static constexpr int kProdBytes = kSeqCache * 8 + kJobRing * (int)sizeof(Job) + kJobRing * (kRows / 8) * 4;
@@ -224,6 +254,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     const uint32_t bar_empty = bar_full + NSTAGE * 8;       // NSTAGE x 8 bytes
     const uint32_t bar_epi_full = bar_empty + NSTAGE * 8;   // consumers -> epilogue
     const uint32_t bar_epi_empty = bar_epi_full + 8;        // epilogue -> consumers
+    const uint32_t bar_cons = bar_epi_empty + 8;            // consumer warps among themselves
     StageDesc* sEpi = reinterpret_cast<StageDesc*>(smem + L::kOffEpi);
     float* sW = reinterpret_cast<float*>(smem + L::kOffW);
     float* sHM = sW + CW * GP;
@@ -250,6 +281,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         }
         mbar_init(bar_epi_full, CW * 32);
         mbar_init(bar_epi_empty, 32);
+        mbar_init(bar_cons, CW * 32);
         fence_mbar_init();
         fence_proxy_async_smem();
     }
@@ -635,7 +667,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         };
         // Descriptor and transaction count of a stage (elected lane).
         auto arm_stage = [&](const Job& job, int stage, unsigned vmask, bool new_tok, int new_r,
-                             int new_row) {
+                             int new_row, bool cta_last) {
             const bool piece_start = job.cb == job.b_lo;
             const bool piece_end = job.cb + job.nblk == job.b_hi;
             // Valid rows: inside the stage, before the context end, in a
@@ -658,7 +690,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             }
             const int flags = (piece_start ? kPieceStart : 0) | (piece_end ? kPieceEnd : 0) |
                               (job.nsplits == 1 ? kPieceComplete : 0) |
-                              (fused && !pos_ok(job) ? kRopeSkip : 0) | (new_tok ? kNewToken : 0);
+                              (fused && !pos_ok(job) ? kRopeSkip : 0) | (new_tok ? kNewToken : 0) |
+                              (cta_last ? kCtaLast : 0);
             if (fused && piece_start && !pos_ok(job)) flag_status(TLB_STATUS_BAD_POSITION);
             int4* dw = reinterpret_cast<int4*>(&sDesc[stage]);
             dw[0] = make_int4((int)rows[0], (int)rows[1], (int)rows[2], (int)rows[3]);
@@ -744,7 +777,10 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 if ((vmask >> b) & 1u) new_row = y + job.pos % bs;
             }
             if (elect_one()) {
-                arm_stage(job, stage, vmask, new_tok, new_r, new_row);
+                // jobs up to k + kPrefetch are in the ring: an invalid next job
+                // means this stage ends the CTA's range
+                arm_stage(job, stage, vmask, new_tok, new_r, new_row,
+                          !sJob[(k + 1) % kJobRing].valid);
                 issue_copies(job, stage, vmask, ys, job.cb == job.b_lo, new_tok);
             }
             __syncwarp();
@@ -960,12 +996,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                             float M = one_chunk ? -INFINITY : sGM[lane];
                             if (one_chunk)
                                 for (int j = 0; j < cn; ++j) M = fmaxf(M, sCW[j * GP + lane]);
-                            float lt = c0 == 0 ? 0.f : sGL[lane];
-                            for (int j = 0; j < cn; ++j) {
-                                const float wt = M == -INFINITY ? 0.f : exp2f(sCW[j * GP + lane] - M);
-                                sCW[j * GP + lane] = wt;
-                                lt += wt * sCL[j * GP + lane];
-                            }
+                            const float lt = piece_weights(sCW + lane, sCL + lane, cn, GP, M,
+                                                           c0 == 0 ? 0.f : sGL[lane]);
                             // after the last chunk: the reciprocal, for the store
                             sGL[lane] = c0 + cn < n ? lt : (lt > 0.f ? 1.f / lt : 0.f);
                         }
@@ -975,10 +1007,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                     for (int i = 0; i < kPer4; ++i) {
                         const int h = min(4 * (lane + 32 * i) / D, GP - 1);
                         const float w0 = sCW[kk * GP + h], w1 = two ? sCW[(kk + 1) * GP + h] : 0.f;
-                        acc[i].x += w0 * v0[i].x + w1 * v1[i].x;
-                        acc[i].y += w0 * v0[i].y + w1 * v1[i].y;
-                        acc[i].z += w0 * v0[i].z + w1 * v1[i].z;
-                        acc[i].w += w0 * v0[i].w + w1 * v1[i].w;
+                        add_pair(acc[i], w0, v0[i], w1, v1[i]);
                     }
                 }
             }
@@ -1079,6 +1108,180 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         fence_proxy_async_smem();  // before the stage's next copy overwrites these rows
         __syncwarp();
     };
+    // The CTA's last piece is finished by the consumer warps themselves once
+    // their (m, l, O) are in the hand-off buffer: no other piece follows it,
+    // so they are free, and the epilogue warp may still be busy with the
+    // piece before it. The four warps combine their partials, and a split
+    // piece that is the last of its (sequence, kv head) to finish merges
+    // every piece with the partials of up to four pieces per thread in
+    // flight at once (a single warp takes one round trip per pair).
+    // Phases are separated by an mbarrier of the consumer threads with
+    // bounded waits; a wait that gives up flags the status and abandons the
+    // piece.
+    uint32_t cphase = 0;
+    auto csync = [&]() -> bool {
+        mbar_arrive(bar_cons);
+        const bool ok = mbar_wait_bounded(bar_cons, cphase);
+        cphase ^= 1;
+        if (!ok && lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
+        return ok;
+    };
+    auto finish_last_piece = [&](const StageDesc& e) {
+        constexpr int NC = CW * 32;
+        constexpr int kGroups = GP * D / 4 / NC;  // float4 groups per thread
+        static_assert(GP * D / 4 % NC == 0, "groups split evenly over the consumer threads");
+        const bool split = !(e.flags & kPieceComplete);
+        const int n = e.nsplits;
+        // the arrival counter, read while the warps combine
+        unsigned seen = 0;
+        if (split && tid == 0) seen = ld_acquire_gpu(p.counters + e.u);
+        if (!csync()) return;  // every warp's (m, l, O) is in shared memory
+        // combine the warps' partials: per head h, M = max_w m_w, weights
+        // 2^(m_w - M), l = sum_w w l_w
+        float4 a[kGroups];
+        float scale[kGroups];
+#pragma unroll
+        for (int j = 0; j < kGroups; ++j) {
+            const int el = 4 * (tid + NC * j), h = el / D, dd = el % D;
+            a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            scale[j] = 0.f;
+            if (h < G) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < CW; ++w) M = fmaxf(M, sM[w * GP + h]);
+                float lt = 0.f;
+#pragma unroll
+                for (int w = 0; w < CW; ++w) {
+                    const float wt = M == -INFINITY ? 0.f : exp2f(sM[w * GP + h] - M);
+                    lt += wt * sL[w * GP + h];
+                    const float4 v = *reinterpret_cast<const float4*>(sO + (w * GP + h) * D + dd);
+                    a[j].x += wt * v.x; a[j].y += wt * v.y; a[j].z += wt * v.z; a[j].w += wt * v.w;
+                }
+                scale[j] = lt;
+            }
+        }
+        const long long out_base = ((long long)e.seq * p.num_heads + (long long)e.kvh * G) * D;
+        if (!split) {
+#pragma unroll
+            for (int j = 0; j < kGroups; ++j) {
+                const int el = 4 * (tid + NC * j);
+                if (el / D < G)
+                    Vec4Out<T>::store(out + out_base + el, a[j], scale[j] > 0.f ? 1.f / scale[j] : 0.f);
+            }
+            return;
+        }
+        float hm = -INFINITY, hl = 0.f;  // (m, l) of head tid of this piece
+        if (tid < G) {
+#pragma unroll
+            for (int w = 0; w < CW; ++w) hm = fmaxf(hm, sM[w * GP + tid]);
+#pragma unroll
+            for (int w = 0; w < CW; ++w) {
+                const float wt = hm == -INFINITY ? 0.f : exp2f(sM[w * GP + tid] - hm);
+                hl += wt * sL[w * GP + tid];
+            }
+        }
+        auto slot_k = [&](int k) -> long long {
+            return 2ll * (e.jfirst + k) + ((k == 0 && e.first_slot1) ? 1 : 0);
+        };
+        int* sDecide = sMisc + 16;  // the prologue's words are long since read
+        // If every other piece has published (counter at n - 1), this one is
+        // the last and merges with its own partial in registers; otherwise
+        // it publishes and takes a ticket.
+        if (tid == 0) *sDecide = seen == (unsigned)(n - 1) ? 1 : 0;
+        if (!csync()) return;  // also: every read of the hand-off buffer is done
+        const bool own_regs = *sDecide != 0;
+        if (own_regs) {
+            if (tid == 0) st_relaxed_gpu(p.counters + e.u, 0u);  // ready for the next launch
+        } else {
+            float* wo = p.ws_o + (long long)e.slot * GP * D;
+#pragma unroll
+            for (int j = 0; j < kGroups; ++j) {
+                const int el = 4 * (tid + NC * j);
+                if (el / D < G) *reinterpret_cast<float4*>(wo + el) = a[j];
+            }
+            if (tid < G) {
+                p.ws_ml[((long long)e.slot * GP + tid) * 2 + 0] = hm;
+                p.ws_ml[((long long)e.slot * GP + tid) * 2 + 1] = hl;
+            }
+            __threadfence();  // every thread's partial stores before the release below
+            if (!csync()) return;
+            if (tid == 0)
+                *sDecide = atomic_inc_acq_rel(p.counters + e.u, (unsigned)(n - 1)) == (unsigned)(n - 1);
+            if (!csync()) return;
+            if (*sDecide == 0) return;
+        }
+        // Merge all n pieces. The first partials are requested first (this
+        // piece's own from registers), then the pieces' (m, l) go through the
+        // hand-off buffer into per-head weights, then every thread sums its
+        // groups over the pieces in pairs, ascending.
+        int own = -1;
+        if (own_regs)
+            for (int k = 0; k < n; ++k)
+                if (slot_k(k) == e.slot) own = k;
+        float* sMW = sO;                // [n][GP] maxima, then weights
+        float* sML = sMW + n * GP;      // [n][GP] sums
+        float* sFL = sML + n * GP;      // [GP] 1 / total
+        constexpr int kBatch = 4;                        // pieces in flight per group and thread
+        constexpr int kPre = kGroups <= 2 ? kBatch : 0;  // the first batch, prefetched
+        float4 vpre[kGroups][kPre > 0 ? kPre : 1];
+        auto piece = [&](int k, int j) -> float4 {
+            const int el = 4 * (tid + NC * j);
+            if (k >= n) return make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k == own) return a[j];
+            return __ldcg(reinterpret_cast<const float4*>(p.ws_o + slot_k(k) * GP * D + el));
+        };
+        if constexpr (kPre > 0) {
+#pragma unroll
+            for (int j = 0; j < kGroups; ++j)
+#pragma unroll
+                for (int q = 0; q < kPre; ++q) vpre[j][q] = piece(q, j);
+        }
+        for (int idx = tid; idx < n * G; idx += NC) {
+            const int k = idx / G, h = idx - (idx / G) * G;
+            if (k == own) continue;  // written below by the thread that holds it
+            const float2 ml =
+                __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot_k(k) * GP + h) * 2));
+            sMW[k * GP + h] = ml.x;
+            sML[k * GP + h] = ml.y;
+        }
+        if (own >= 0 && tid < G) {
+            sMW[own * GP + tid] = hm;
+            sML[own * GP + tid] = hl;
+        }
+        if (!csync()) return;
+        if (tid < G) {
+            float M = -INFINITY;
+            for (int k = 0; k < n; ++k) M = fmaxf(M, sMW[k * GP + tid]);
+            const float lt = piece_weights(sMW + tid, sML + tid, n, GP, M, 0.f);
+            sFL[tid] = lt > 0.f ? 1.f / lt : 0.f;
+        }
+        if (!csync()) return;
+#pragma unroll
+        for (int j = 0; j < kGroups; ++j) {
+            const int el = 4 * (tid + NC * j), h = el / D;
+            if (h >= G) continue;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k0 = 0; k0 < n; k0 += kBatch) {
+                float4 v[kBatch];
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) {
+                    if constexpr (kPre > 0)
+                        v[q] = k0 == 0 ? vpre[j][q] : piece(k0 + q, j);
+                    else
+                        v[q] = piece(k0 + q, j);
+                }
+#pragma unroll
+                for (int q = 0; q < kBatch; q += 2) {
+                    const int k = k0 + q;
+                    if (k < n)
+                        add_pair(acc, sMW[k * GP + h], v[q], k + 1 < n ? sMW[(k + 1) * GP + h] : 0.f,
+                                 v[q + 1]);
+                }
+            }
+            Vec4Out<T>::store(out + out_base + el, acc, sFL[h]);
+        }
+    };
+
     while (true) {
         bool got = true;
         got = mbar_wait_bounded(bar_full + 8 * stage, phase);
@@ -1314,6 +1517,10 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 base[8] = o[nt][mt][2];
                 base[D + 8] = o[nt][mt][3];
             }
+        if ((d.flags & kCtaLast) && d.nsplits <= kConsumerMergeMax) {
+            finish_last_piece(d);
+            continue;  // the next stage is the terminate
+        }
         if (tid == 0) *sEpi = d;
         mbar_arrive(bar_epi_full);
         ephase ^= 1;
