@@ -146,6 +146,12 @@ __device__ __forceinline__ void add_pair(float4& a, float w0, const float4& v0, 
 // sit in the hand-off buffer meanwhile); a unit cut into more goes to the
 // epilogue warp.
 constexpr int kConsumerMergeMax = 64;
+// With head dim 64 a piece's partial is half as large and the epilogue
+// warp's merge correspondingly quicker: there the consumer warps take a
+// CTA's last piece only when its unit is cut into at least this many pieces
+// (measured on the shape sweep: fewer pieces lose more to the consumers'
+// barrier phases than the wider merge wins).
+constexpr int kConsumerMinPieces64 = 8;
 
 #ifndef TLB_ATTN_TPW64
 #define TLB_ATTN_TPW64 2
@@ -1517,7 +1523,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 base[8] = o[nt][mt][2];
                 base[D + 8] = o[nt][mt][3];
             }
-        if ((d.flags & kCtaLast) && d.nsplits <= kConsumerMergeMax) {
+        if ((d.flags & kCtaLast) && d.nsplits <= kConsumerMergeMax &&
+            (D == 128 || d.nsplits >= kConsumerMinPieces64)) {
             finish_last_piece(d);
             continue;  // the next stage is the terminate
         }
