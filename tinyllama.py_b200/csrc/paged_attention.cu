@@ -156,7 +156,7 @@ constexpr int kConsumerMinPieces64 = 8;
 #ifndef TLB_ATTN_TPW64
 #define TLB_ATTN_TPW64 2
 #endif
-template <int D, int NT, int NSTAGE, int CW>
+template <int D, int NT, int NSTAGE, int CW, bool FUSED>
 struct TcLayout {
     // 16-token tiles each consumer warp takes per stage: head dim 64 takes two,
     // so a stage carries as many bytes (32 KB of K and V) as with head dim 128
@@ -167,7 +167,7 @@ struct TcLayout {
     static constexpr int kStageKV = kRows * D * 2;  // bytes of K (or V) per stage
     // query group of the piece, then (fused decode step) the cos/sin row of
     // the new token's position and that token's raw key and value rows
-    static constexpr int kQBytes = 8 * NT * D * 2 + 3 * D * 2;
+    static constexpr int kQBytes = 8 * NT * D * 2 + (FUSED ? 3 * D * 2 : 0);
     static constexpr int kGP = 8 * NT;                 // padded heads per piece
     static constexpr int kOFloats = CW * kGP * D;
     static constexpr int kOffK = 0;
@@ -236,11 +236,11 @@ __device__ __forceinline__ long long range_start(int j, long long W, int P) {
 }  // namespace
 
 // One head tile (NT == 1) keeps two CTAs per SM: at most 168 registers.
-template <typename T, int D, int NT, int NSTAGE, int CW>
+template <typename T, int D, int NT, int NSTAGE, int CW, bool FUSED>
 __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     paged_attention_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
-    using L = TcLayout<D, NT, NSTAGE, CW>;
+    using L = TcLayout<D, NT, NSTAGE, CW, FUSED>;
     constexpr int ROWS = L::kRows;        // tokens per stage
     constexpr int kBpsMax = ROWS / 8;     // most KV blocks in a stage (block_size >= 8)
     constexpr int kCS = kCostStage * ROWS / 64;  // cost of one stage of ROWS tokens
@@ -460,7 +460,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     if (warp == CW) {
         // ===================================================== producer warp
         const uint64_t pol = l2_policy_evict_first();
-        const bool fused = p.cos_sin != nullptr;
+        constexpr bool fused = FUSED;  // p.cos_sin != nullptr
         const T* cos_sin = reinterpret_cast<const T*>(p.cos_sin);
         const T* key_new = reinterpret_cast<const T*>(p.key_new);
         const T* value_new = reinterpret_cast<const T*>(p.value_new);
@@ -703,7 +703,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             dw[0] = make_int4((int)rows[0], (int)rows[1], (int)rows[2], (int)rows[3]);
             dw[1] = make_int4(flags, job.s, job.h, 2 * job.item + (job.first ? 0 : 1));
             dw[2] = make_int4(job.nsplits, job.jfirst, job.first_slot1, job.s * KVH + job.h);
-            dw[3] = make_int4(new_r, new_row, 0, 0);
+            if (FUSED) dw[3] = make_int4(new_r, new_row, 0, 0);
             // KV tiles, the query group and cos/sin row of a piece start, the
             // new token's key and value rows (and cos/sin row) of its stage
             const uint32_t bytes = (uint32_t)__popc(vmask) * (uint32_t)bs * D * 2u * 2u +
@@ -1055,7 +1055,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     int stage = 0;
     uint32_t phase = 0;
     uint32_t ephase = 0;
-    const bool fused_q = p.cos_sin != nullptr;
+    constexpr bool fused_q = FUSED;
     T* key_new = reinterpret_cast<T*>(p.key_new);
     T* kc_new = reinterpret_cast<T*>(p.key_cache);
     T* vc_new = reinterpret_cast<T*>(p.value_cache);
@@ -1339,7 +1339,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         for (int t = 0; t < TPW; ++t) {
         const int r0 = (t * CW + warp) * kTileRows;
         const uint32_t ld_off = ld_off_t[t];
-        if ((d.flags & kNewToken) &&
+        if (FUSED && (d.flags & kNewToken) &&
             (d.new_r >= 0 ? d.new_r / kTileRows == t * CW + warp : (t == 0 && warp == 0)))
             write_new_token(stage, d);
         // Valid rows of this 16-token tile.
@@ -1660,11 +1660,11 @@ __global__ void __launch_bounds__(256) paged_attention_generic_kernel(const Gene
 // ============================================================ host side
 namespace {
 
-template <typename T, int D, int NT, int NSTAGE, int CW>
+template <typename T, int D, int NT, int NSTAGE, int CW, bool FUSED>
 cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensorMap& tv,
                         int grid, bool overlap, cudaStream_t st) {
-    using L = TcLayout<D, NT, NSTAGE, CW>;
-    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE, CW>;
+    using L = TcLayout<D, NT, NSTAGE, CW, FUSED>;
+    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE, CW, FUSED>;
     static std::once_flag once[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1688,10 +1688,12 @@ cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap& tk, const CUtensor
     return cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
 }
 
+// Occupancy of the fused instance, whose shared memory is the larger: the
+// grid it sizes fits both instances.
 template <typename T, int D, int NT, int NSTAGE, int CW>
 int occupancy_t() {
-    using L = TcLayout<D, NT, NSTAGE, CW>;
-    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE, CW>;
+    using L = TcLayout<D, NT, NSTAGE, CW, true>;
+    auto kern = paged_attention_tc_kernel<T, D, NT, NSTAGE, CW, true>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) !=
         cudaSuccess)
         return 0;
@@ -1724,15 +1726,24 @@ constexpr int kStages128 = TLB_ATTN_STAGES_128;
 constexpr int kCw1 = TLB_ATTN_CW1;        // head_dim 128
 constexpr int kCw1_64 = TLB_ATTN_CW1_64;  // head_dim 64
 
+// The fused decode step (cos/sin table given) and plain attention are
+// separate instances, so plain attention carries none of the fused code.
+template <typename T, bool FUSED>
+cudaError_t dispatch_tc_f(int head_dim, int group, const TcParams& p, const CUtensorMap& tk,
+                          const CUtensorMap& tv, int grid, bool ov, cudaStream_t st) {
+    const bool two = group > 8;
+    if (head_dim == 64)
+        return two ? launch_tc_t<T, 64, 2, kStages64, kConsumerWarps, FUSED>(p, tk, tv, grid, ov, st)
+                   : launch_tc_t<T, 64, 1, kStages64, kCw1_64, FUSED>(p, tk, tv, grid, ov, st);
+    return two ? launch_tc_t<T, 128, 2, kStages128, kConsumerWarps, FUSED>(p, tk, tv, grid, ov, st)
+               : launch_tc_t<T, 128, 1, kStages128, kCw1, FUSED>(p, tk, tv, grid, ov, st);
+}
+
 template <typename T>
 cudaError_t dispatch_tc(int head_dim, int group, const TcParams& p, const CUtensorMap& tk,
                         const CUtensorMap& tv, int grid, bool ov, cudaStream_t st) {
-    const bool two = group > 8;
-    if (head_dim == 64)
-        return two ? launch_tc_t<T, 64, 2, kStages64, kConsumerWarps>(p, tk, tv, grid, ov, st)
-                   : launch_tc_t<T, 64, 1, kStages64, kCw1_64>(p, tk, tv, grid, ov, st);
-    return two ? launch_tc_t<T, 128, 2, kStages128, kConsumerWarps>(p, tk, tv, grid, ov, st)
-               : launch_tc_t<T, 128, 1, kStages128, kCw1>(p, tk, tv, grid, ov, st);
+    return p.cos_sin != nullptr ? dispatch_tc_f<T, true>(head_dim, group, p, tk, tv, grid, ov, st)
+                                : dispatch_tc_f<T, false>(head_dim, group, p, tk, tv, grid, ov, st);
 }
 
 template <typename T>
