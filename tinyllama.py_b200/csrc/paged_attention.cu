@@ -1111,8 +1111,9 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             reinterpret_cast<uint4*>(vc_new + grow)[u] = v;
             *reinterpret_cast<uint4*>(smem + L::kOffV + stg * L::kStageKV + unit_off(u)) = v;
         }
-        fence_proxy_async_smem();  // before the stage's next copy overwrites these rows
-        __syncwarp();
+        // The proxy fence that orders these generic writes before the
+        // stage's next copy, and the warp barrier before the tile's reads,
+        // come after the call (shared with the zeroing of unused V rows).
     };
     // The CTA's last piece is finished by the consumer warps themselves once
     // their (m, l, O) are in the hand-off buffer: no other piece follows it,
@@ -1314,11 +1315,15 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 // with the cos/sin row that came with it. Columns c and
                 // c + D/2 of a fragment word sit in k-steps ks and ks + KS/2
                 // of the same lane, so each lane rotates its own pairs.
+                // Words 1 and 3 hold head g + 8, words 0 and 2 head g: heads
+                // at or beyond the group are zero padding and stay zero.
                 const T* cs = sq + GP * D;
 #pragma unroll
                 for (int ks = 0; ks < KS / 2; ++ks)
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
+                        if (NT == 1 && (r & 1)) continue;  // head g + 8 >= 8 >= G
+                        if ((r & 1) ? g + 8 >= G : g >= G) continue;
                         const int col = ks * 16 + 2 * q4 + (r >= 2 ? 8 : 0);
                         rope_packed2<T>(qa[ks][r], qa[ks + KS / 2][r],
                                         *reinterpret_cast<const uint32_t*>(cs + col),
@@ -1339,11 +1344,16 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         for (int t = 0; t < TPW; ++t) {
         const int r0 = (t * CW + warp) * kTileRows;
         const uint32_t ld_off = ld_off_t[t];
-        if (FUSED && (d.flags & kNewToken) &&
-            (d.new_r >= 0 ? d.new_r / kTileRows == t * CW + warp : (t == 0 && warp == 0)))
-            write_new_token(stage, d);
         // Valid rows of this 16-token tile.
         const unsigned vmask = (sDesc[stage].rows[r0 >> 5] >> (r0 & 31)) & 0xffffu;
+        if (FUSED && (d.flags & kNewToken) &&
+            (d.new_r >= 0 ? d.new_r / kTileRows == t * CW + warp : (t == 0 && warp == 0))) {
+            write_new_token(stage, d);
+            if (vmask == 0u || vmask == 0xffffu) {  // no zeroing below to share the fence
+                fence_proxy_async_smem();  // before the stage's next copy overwrites the rows
+                __syncwarp();
+            }
+        }
 
         if (vmask != 0u) {
             const uint32_t kbase = sbase + L::kOffK + stage * L::kStageKV;
