@@ -241,3 +241,24 @@ def test_counters_are_zero_after_every_launch(H, KVH, D, bs, lens, built_lib):
     torch.cuda.synchronize()
     ws = A._workspaces[(torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream)]
     assert ws.clean > 0 and int(ws.buf[:ws.clean].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("lens,H,KVH,D", [
+    ("qwen3b", 16, 2, 128),                 # the 3B decode batch: many two- to five-piece splits
+    ([8192, 8192, 300, 5000], 14, 2, 64),   # head dim 64, units cut into 8+ pieces
+    ([20000], 16, 2, 128),                  # more pieces than the consumer warps merge
+])
+def test_split_merges_give_the_same_bits_every_launch(lens, H, KVH, D, built_lib):
+    """Which piece of a split (sequence, kv head) finishes last changes from
+    launch to launch, and with it the warps that merge: the epilogue warp or
+    the consumer warps of a CTA whose last piece it was. Both use the same
+    arithmetic in the same order, so every launch gives the same bits."""
+    if lens == "qwen3b":
+        batch = W.make_batch(W.qwen3b_decode(5, batch=64))
+    else:
+        batch = _custom_batch(lens, H, KVH, D, 16, "bfloat16")
+    first = _attend(batch)
+    for i in range(30):
+        out = _attend(batch)
+        assert torch.equal(out.view(torch.int16), first.view(torch.int16)), f"launch {i}"
+    assert _lib.device_status() == 0
