@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample budget (rank 0, N=1)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-group", type=int, default=4,
+                    help="e2e: consecutive steps whose inputs share one host-to-device copy "
+                         "(rounded to a multiple of --layers; 4 measured best of 4, 8, 12)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="rotating independent KV pools per GPU (profiling runs use 1)")
     ap.add_argument("--sweep", action="store_true",
@@ -388,11 +391,14 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
     maxB = max(b.block_tables.shape[1] for b in layers)
     layout, total = pack_layout(S, H, KVH, D, maxB)
     nl = len(layers)
-    # Host inputs of the nl layers, back to back in one pinned buffer, and two
-    # device staging banks of the same size.
-    host = torch.zeros(nl * total, dtype=torch.uint8).pin_memory()
-    for r, b in enumerate(layers):
-        h = host[r * total:(r + 1) * total]
+    # A group of gs consecutive steps (a multiple of nl: step j of a group
+    # runs layer j % nl): its inputs back to back in one pinned host buffer,
+    # and two device staging banks of the same size.
+    gs = nl * max(1, getattr(args, "e2e_group", 4) // nl)
+    host = torch.zeros(gs * total, dtype=torch.uint8).pin_memory()
+    for j in range(gs):
+        b = layers[j % nl]
+        h = host[j * total:(j + 1) * total]
 
         def put(name, t):
             o, n = layout[name]
@@ -402,7 +408,7 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
         bt[:, : b.block_tables.shape[1]] = b.block_tables.cpu()
         put("query", b.query); put("key", b.key); put("value", b.value)
         put("tables", bt); put("lens", b.seq_lens)
-    banks = torch.empty(2, nl * total, dtype=torch.uint8, device=dev)
+    banks = torch.empty(2, gs * total, dtype=torch.uint8, device=dev)
 
     def views_of(bank, r):
         d = banks[bank, r * total:(r + 1) * total]
@@ -417,10 +423,10 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
                     tables=view("tables", torch.int32, (S, maxB)),
                     lens=view("lens", torch.int32, (S,)))
 
-    views = [[views_of(k, r) for r in range(nl)] for k in range(2)]
+    views = [[views_of(k, j) for j in range(gs)] for k in range(2)]
     # A decode pass as a serving engine runs it: the public-API calls of a
     # 36-layer model's pass (Qwen2.5-3B has 36 layers) captured once into a
-    # CUDA graph. The steps go in groups of nl consecutive layers: one pinned
+    # CUDA graph. The steps go in groups of gs consecutive steps: one pinned
     # host-to-device copy brings a group's inputs into a staging bank (two
     # banks, so a group's copy overlaps the previous group's compute), the
     # group's steps run back to back with programmatic overlap (each kernel
@@ -428,8 +434,8 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
     # dependency, wrote - before it waits for the kernel ahead of it), and
     # the group's outputs are read back on their own stream while the next
     # group computes. Every step's inputs and output cross PCIe every replay.
-    groups = -(-36 // nl)
-    per_graph = groups * nl
+    groups = -(-36 // gs)
+    per_graph = groups * gs
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     outs = [torch.empty(S, H, D, dtype=torch.bfloat16).pin_memory() for _ in range(per_graph)]
 
@@ -449,8 +455,8 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
                 ready.record(s_in)
             stream.wait_event(ready)
             produced = []
-            for r in range(nl):
-                b, v = layers[r], views[bank][r]
+            for j in range(gs):
+                b, v = layers[j % nl], views[bank][j]
                 produced.append(A.paged_attention_with_rope(
                     v["query"], v["key"], v["value"], b.key_cache, b.value_cache, v["tables"],
                     v["lens"], b.cos_sin_cache, b.scale, overlap_prologue=True))
@@ -459,8 +465,8 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
             done.append(ev)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev)
-                for r, out in enumerate(produced):
-                    outs[gi * nl + r].copy_(out, non_blocking=True)
+                for j, out in enumerate(produced):
+                    outs[gi * gs + j].copy_(out, non_blocking=True)
         join_in, join_out = torch.cuda.Event(), torch.cuda.Event()
         join_in.record(s_in)
         join_out.record(s_out)
@@ -500,9 +506,9 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
             "steps": steps,
             "path": "cscr.attention.paged_attention_with_rope (RoPE + cache write + attention, "
                     "overlap_prologue=True), per step its inputs host-to-device from pinned memory "
-                    f"(one copy per group of {nl} consecutive steps, double-buffered) and its "
+                    f"(one copy per group of {gs} consecutive steps, double-buffered) and its "
                     f"output device-to-host, copies on their own streams; {per_graph} steps "
-                    "(a 36-layer decode pass) per CUDA-graph replay"}
+                    "(a 36-layer decode pass, rounded up to whole groups) per CUDA-graph replay"}
 
 
 # ------------------------------------------------------------ CPU side
