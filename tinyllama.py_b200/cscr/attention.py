@@ -160,6 +160,11 @@ def paged_attention_with_rope(query: torch.Tensor, key: torch.Tensor, value: tor
     (rotated in place), value likewise, cos_sin_cache [rows, head_dim] in the
     query dtype. Shapes the tensor-core kernel does not serve run as those two
     launches.
+
+    ``overlap_prologue`` has the contract of ``paged_attention``'s: set it
+    only when the kernel launched just before on this stream writes neither
+    block_tables nor seq_lens (query, key, value and the caches are read only
+    after that kernel has finished).
     """
     torch_check(query.is_cuda and key.is_cuda and value.is_cuda and cos_sin_cache.is_cuda,
                 "query, key, value and cos_sin_cache must be CUDA tensors")
