@@ -103,3 +103,24 @@ def test_build_flags_target_sm100a_only():
 
     assert B.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
     assert "-lineinfo" in B.NVCC_FLAGS
+
+
+def test_fused_step_argument_errors_without_gpu(built_lib):
+    """tlb_paged_attention_with_rope rejects bad arguments, and shapes the
+    fused kernel does not serve, before any CUDA call."""
+    from cscr import _lib
+
+    lib = _lib.load()
+    p = 1 << 12  # stands in for 16-byte aligned device pointers; nothing is dereferenced
+
+    def call(num_seqs=4, head_dim=128, dtype=2, cache_rows=4096, key_stride=256):
+        return lib.tlb_paged_attention_with_rope(
+            p, p, p, p, p, p, p, p, p, cache_rows, num_seqs, 16, 2, head_dim, 10, 16, 4,
+            key_stride, 256, 0.125, dtype, None, 0, 0, None)
+
+    assert call(num_seqs=0) == 1 and "at least one sequence" in _lib.last_error()
+    assert call(cache_rows=0) == 1 and "at least one row" in _lib.last_error()
+    assert call(key_stride=100) == 1
+    # fp32 and head dim 96 are served by the two-launch form, which the op falls back to
+    assert call(dtype=0) == _lib.TLB_ERR_UNSUPPORTED and "tensor-core path" in _lib.last_error()
+    assert call(head_dim=96, key_stride=192) == _lib.TLB_ERR_UNSUPPORTED
