@@ -146,6 +146,16 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def prime(self, busy, timeout_s: float = 3.0) -> int:
+        """Keep the GPU busy with `busy()` (untimed) until the sampler's first
+        line arrives, so that short timed regions still get samples under load.
+        Returns how many times `busy` ran."""
+        n, t0 = 0, time.perf_counter()
+        while self.proc is not None and not self.lines and time.perf_counter() - t0 < timeout_s:
+            busy()
+            n += 1
+        return n
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -253,44 +263,57 @@ def run_ours(args, rank, world, local):
             for b in layers:
                 attn_only(b)
 
-    reps = max(1, args.steps // nl)
-    steps = reps * nl
-    wreps = max(1, math.ceil(args.warmup / nl))
+    # Exactly K timed steps: K // nl replays of the nl-layer graph, then the
+    # remaining K % nl steps launched directly; exactly W warm-up steps.
+    steps = max(1, args.steps)
+    reps, rest = divmod(steps, nl)
+    warm = max(0, args.warmup)
 
-    def timed(graph, n):
+    def timed(graph, fn, n_reps, n_rest):
         with torch.cuda.stream(stream):
-            for _ in range(wreps):
-                graph.replay()
+            for i in range(warm):
+                fn(layers[i % nl])
         stream.synchronize()
         barrier()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             e0.record(stream)
-            for _ in range(n):
+            for _ in range(n_reps):
                 graph.replay()
+            for i in range(n_rest):
+                fn(layers[i])
             e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
-        ms = e0.elapsed_time(e1)
+        own = e0.elapsed_time(e1)
+        ms = own
         if world > 1:
             t = torch.tensor([ms], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = t.item()
-        return ms
+        return ms, own
 
     devices = list(range(world)) if world > 1 else [local]
+    # clocks: sampled from before the warm-up to the end of the e2e leg
     sampler = ClockSampler(devices) if rank == 0 else None
+    primed = 0
     if sampler:
         sampler.__enter__()
-    step_ms = timed(g_step, reps)
-    if sampler:
-        sampler.__exit__(None, None, None)
-    attn_ms = timed(g_attn, reps)
+
+        def busy():
+            with torch.cuda.stream(stream):
+                for _ in range(50):
+                    g_step.replay()
+            stream.synchronize()
+
+        primed = sampler.prime(busy) * 50 * nl
+    step_ms, own_step_ms = timed(g_step, step, reps, rest)
+    attn_ms, _ = timed(g_attn, attn_only, reps, rest)
 
     # spread: 20 samples of the step, each over a slice of the replays
     nsamp = 20
-    per = max(1, reps // nsamp)
+    per = max(1, max(reps, 1) // nsamp)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(nsamp + 1)]
     with torch.cuda.stream(stream):
         evs[0].record(stream)
@@ -311,6 +334,9 @@ def run_ours(args, rank, world, local):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, layers, step, stream, dev, world, barrier, rank)
+        e2e["eager"] = run_e2e_eager(args, layers, dev, world, barrier)
+    if sampler:
+        sampler.__exit__(None, None, None)
 
     tokens_per_step = 64 * world
     value = tokens_per_step * steps / (step_ms / 1e3)
@@ -318,6 +344,19 @@ def run_ours(args, rank, world, local):
     attn_bytes = statistics.fmean(
         R.attention_bytes(l, spec0.block_size, H, KVH, D, 2) for l in lens_all)
     rope_bytes = R.rope_bytes(S, H, KVH, D, D, 2) + R.cache_write_bytes(S, KVH, D, 2)
+    # every rank's own step time and bytes: what limits the N-GPU curve
+    mine = torch.tensor([own_step_ms * 1e3 / steps, attn_bytes + rope_bytes,
+                         float(sum(int(l.sum()) for l in lens_all) / nl)],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+    else:
+        gathered = [mine]
+    per_rank = [{"rank": r, "us_per_step": round(float(g[0]), 3),
+                 "bytes_per_step": int(g[1]), "context_tokens": int(g[2]),
+                 "gbs": round(float(g[1]) / (float(g[0]) * 1e-6) / 1e9, 1)}
+                for r, g in enumerate(x.cpu() for x in gathered)]
     t_attn_us = attn_ms * 1e3 / steps
     t_step_us = step_ms * 1e3 / steps
     # the step is one launch of the fused kernel: its bytes over its time
@@ -332,7 +371,7 @@ def run_ours(args, rank, world, local):
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
-        "steps": steps, "warmup": wreps * nl, "ms_per_step": round(step_ms / steps, 6),
+        "steps": steps, "warmup": warm, "ms_per_step": round(step_ms / steps, 6),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v and KV pool, seeded lengths)",
         "config": {"workload": WORKLOAD, "global_batch": tokens_per_step, "seq_len": "U[128,4096]",
@@ -341,7 +380,8 @@ def run_ours(args, rank, world, local):
                    "l2": f"{nl} rotating independent KV pools per GPU "
                          f"(~{nl * attn_bytes / 1e6:.0f} MB of KV per rotation > 126 MB L2)",
                    "timed_region": "CUDA-graph replay of the decode step: RoPE + KV-cache write "
-                                   "+ paged attention in one launch per layer"},
+                                   "+ paged attention in one launch per layer",
+                   "clock_priming_steps": primed},
         "hbm_gbs_step": round((attn_bytes + rope_bytes) / (t_step_us * 1e-6) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round((attn_bytes + rope_bytes) / (t_step_us * 1e-6) / 1e9
                                        / NOMINAL_HBM_GBS, 4),
@@ -360,6 +400,7 @@ def run_ours(args, rank, world, local):
         "step_us_p10_p50_p90": [round(q10, 3), round(q50, 3), round(q90, 3)],
         "gpu_launches": steps * world,
         "gpu_launches_per_rank": steps,
+        "per_rank": per_rank,
         "clocks": sampler.summary() if sampler else None,
     }
     if e2e is not None:
@@ -509,6 +550,78 @@ def run_e2e(args, layers, step_fn, stream, dev, world, barrier, rank):
                     f"(one copy per group of {gs} consecutive steps, double-buffered) and its "
                     f"output device-to-host, copies on their own streams; {per_graph} steps "
                     "(a 36-layer decode pass, rounded up to whole groups) per CUDA-graph replay"}
+
+
+def run_e2e_eager(args, layers, dev, world, barrier):
+    """The same steps through the public op, launched one by one from Python
+    (no CUDA graph): per step one pinned host-to-device copy of that step's
+    inputs, the op, and a device-to-host copy of its output, all on one
+    stream. Includes the per-call host cost (argument checks, ctypes) that a
+    caller who does not capture graphs pays."""
+    import torch.distributed as dist
+
+    from cscr import attention as A
+
+    spec0 = layers[0].spec
+    S, H, KVH, D = len(spec0.seq_lens), spec0.num_heads, spec0.num_kv_heads, spec0.head_dim
+    maxB = max(b.block_tables.shape[1] for b in layers)
+    layout, total = pack_layout(S, H, KVH, D, maxB)
+    nl = len(layers)
+    hosts = []
+    for b in layers:
+        h = torch.zeros(total, dtype=torch.uint8).pin_memory()
+
+        def put(name, t):
+            o, n = layout[name]
+            h[o:o + n].copy_(t.contiguous().view(torch.uint8).view(-1).cpu())
+
+        bt = torch.zeros(S, maxB, dtype=torch.int32)
+        bt[:, : b.block_tables.shape[1]] = b.block_tables.cpu()
+        put("query", b.query); put("key", b.key); put("value", b.value)
+        put("tables", bt); put("lens", b.seq_lens)
+        hosts.append(h)
+    d = torch.empty(total, dtype=torch.uint8, device=dev)
+
+    def view(name, dtype, shape):
+        o, n = layout[name]
+        return d[o:o + n].view(dtype).view(*shape)
+
+    q, k = view("query", torch.bfloat16, (S, H, D)), view("key", torch.bfloat16, (S, KVH * D))
+    v, t = view("value", torch.bfloat16, (S, KVH, D)), view("tables", torch.int32, (S, maxB))
+    lens = view("lens", torch.int32, (S,))
+    out_h = torch.empty(S, H, D, dtype=torch.bfloat16).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def one(i):
+        b = layers[i % nl]
+        d.copy_(hosts[i % nl], non_blocking=True)
+        out = A.paged_attention_with_rope(q, k, v, b.key_cache, b.value_cache, t, lens,
+                                          b.cos_sin_cache, b.scale)
+        out_h.copy_(out, non_blocking=True)
+
+    n = max(1, min(args.steps, 2000))
+    for i in range(max(args.warmup, 1)):
+        one(i)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n):
+        one(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = tt.item()
+    return {"value": round(S * world * n / (ms / 1e3), 1), "unit": UNIT, "steps": n,
+            "h2d_bytes_per_step": int(total), "d2h_bytes_per_step": int(S * H * D * 2),
+            "us_per_step": round(ms * 1e3 / n, 2),
+            "path": "cscr.attention.paged_attention_with_rope called from Python once per step, "
+                    "no CUDA graph; per step one pinned H2D copy of its inputs and a D2H copy "
+                    "of its output on the same stream"}
 
 
 # ------------------------------------------------------------ CPU side

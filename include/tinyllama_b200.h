@@ -69,8 +69,23 @@ TLB_API const char* tlb_version(void);
 
 /* Reads (and, if clear != 0, resets) the status word of the current device.
  * Enqueued on `stream` and waits for it: a debugging aid, not a hot-path
- * call. */
+ * call. When it reports TLB_STATUS_WAIT_TIMEOUT, the static scratch of
+ * tlb_paged_attention_no_alloc on this device is cleared again before its next
+ * use; a caller that owns an attention workspace must re-zero its counter
+ * prefix itself (a kernel that gave up a wait may leave counters set). */
 TLB_API int tlb_get_device_status(uint32_t* status_out, int clear, void* stream);
+
+/* Bounded waits of the tensor-core attention kernels. Every wait of the
+ * kernel's pipeline (a stage's data, a free stage, a hand-off between warps,
+ * a phase of the merge) gives up after `tries` mbarrier probes, sets
+ * TLB_STATUS_WAIT_TIMEOUT, lets the copies it already issued land and
+ * returns; no kernel waits without bound. TLB_WAIT_LIMIT_DEFAULT (the value
+ * in force until this is called) is far above any legitimate wait. Smaller
+ * values are a failure-injection aid for tests (0: every such wait gives up
+ * at once). Process-wide; applies to launches issued after the call. No
+ * reference counterpart (the reference kernels do not wait). */
+#define TLB_WAIT_LIMIT_DEFAULT (1u << 22)
+TLB_API int tlb_attention_set_wait_limit(uint32_t tries);
 
 /* ------------------------------------------------------------------------
  * Paged attention (decode: one query token per sequence).

@@ -108,6 +108,13 @@ def paged_attention(query, key_cache, value_cache, block_tables, seq_lens, scale
     sequence's blocks, keep its first seq_len tokens, fold query heads onto
     their KV head (h // (H / KVH)), fp32 softmax(scale q K^T) V, cast once.
     """
+    return from_f32(paged_attention_f32(query, key_cache, value_cache, block_tables, seq_lens,
+                                        scale, dtype, threads), dtype)
+
+
+def paged_attention_f32(query, key_cache, value_cache, block_tables, seq_lens, scale, dtype,
+                        threads: int | None = None) -> np.ndarray:
+    """paged_attention's fp32 result before the final cast (the tolerance reference)."""
     S, H, D = query.shape
     NB, KVH, BS, Dk = key_cache.shape
     assert Dk == D and H % KVH == 0
@@ -126,7 +133,7 @@ def paged_attention(query, key_cache, value_cache, block_tables, seq_lens, scale
     else:
         with ThreadPoolExecutor(max_workers=threads) as ex:
             list(ex.map(work, range(S)))
-    return from_f32(out, dtype)
+    return out
 
 
 def paged_attention_threads(query, key_cache, value_cache, block_tables, seq_lens, scale, dtype,
@@ -271,7 +278,7 @@ def ceil_div(a, b):
 
 __all__ = [
     "DTYPES", "bf16_bits_to_f32", "f32_to_bf16_bits", "to_f32", "from_f32", "storage_np_dtype",
-    "paged_attention", "paged_attention_threads", "rotary_embedding_neox", "cos_sin_cache",
+    "paged_attention", "paged_attention_f32", "paged_attention_threads", "rotary_embedding_neox", "cos_sin_cache",
     "write_kv_cache", "reshape_and_cache", "decode_metadata", "copy_blocks", "swap_blocks",
     "ceil_div",
 ]

@@ -49,6 +49,17 @@ def check_attention(batch: W.DecodeBatch, out: torch.Tensor, seqs=None, query=No
     np.testing.assert_allclose(O.to_f32(got, dtype), ref, **tol_for(dtype))
 
 
+def oracle_f32_from_tensors(query, key_cache, value_cache, block_tables, seq_lens, scale, dtype):
+    """fp32 oracle output for device tensors of one attention call (pool compacted)."""
+    from types import SimpleNamespace
+
+    view = SimpleNamespace(block_tables=block_tables, seq_lens=seq_lens, key_cache=key_cache,
+                           value_cache=value_cache,
+                           spec=SimpleNamespace(block_size=key_cache.shape[2]))
+    kc, vc, tables, lens = W.compact_for_oracle(view)
+    return oracle_attention_f32(W.to_numpy(query), kc, vc, tables, lens, scale, dtype)
+
+
 def _subset(batch: W.DecodeBatch, seqs):
     sub = W.DecodeBatch(**{**batch.__dict__})
     sub.block_tables = batch.block_tables[list(seqs)]

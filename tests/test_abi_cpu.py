@@ -65,6 +65,24 @@ def test_argument_errors_without_gpu(built_lib):
     assert size.value >= 64 * 2 * 4
 
 
+def test_no_alloc_checks_arguments_before_touching_its_scratch(built_lib):
+    """The allocation-free entry point runs every argument check of the
+    workspace entry point before it clears or uses its static array: a bad
+    call (here a null output, with far more sequences than the array could
+    serve, fp32 and bf16) is refused with no CUDA call at all, so it also
+    fails cleanly on a host without a GPU."""
+    from cscr import _lib
+
+    lib = _lib.load()
+    for dtype in (0, 2):
+        rc = lib.tlb_paged_attention_no_alloc(None, 256, 256, 256, 256, 256, 5_000_000, 16, 2,
+                                              128, 10, 16, 4, 0.1, dtype, 0, None)
+        assert rc == 1 and "must not be null" in _lib.last_error()
+    rc = lib.tlb_paged_attention_no_alloc(256, 256, 256, 256, 256, 256, 4, 16, 2, 128, 10, 16, 4,
+                                          0.1, 2, 0x80, None)
+    assert rc == 1 and "unknown flags" in _lib.last_error()
+
+
 def test_reference_messages_on_cpu_tensors():
     from cscr import attention as A
     from cscr import pos_encoding as PE

@@ -80,9 +80,7 @@ def test_long_tail_bs32_high_block_ids(built_lib):
     batch = W.make_batch(spec)
     assert batch.block_tables.max().item() * 16 * 1024 > 2 ** 31
     out = _attend(batch)
-    order = np.argsort(lens)
-    seqs = sorted(set(order[-6:].tolist() + order[:6].tolist() + list(range(0, 256, 37))))
-    check_attention(batch, out, seqs=seqs)
+    check_attention(batch, out)  # every one of the 256 sequences
 
 
 @pytest.mark.parametrize("heads", ["qwen0.5b", "qwen3b"])
@@ -93,9 +91,7 @@ def test_long_tail_bs32_high_block_ids(built_lib):
 def test_sweep_point(block_size, batch_size, context, dtype, heads, built_lib):
     spec = W.sweep_point(block_size, batch_size, context, dtype, heads)
     batch = W.make_batch(spec)
-    out = _attend(batch)
-    seqs = list(range(batch_size)) if batch_size <= 8 else [0, 1, batch_size // 2, batch_size - 1]
-    check_attention(batch, out, seqs=seqs)
+    check_attention(batch, _attend(batch))  # every sequence of the point
 
 
 def _custom_batch(lens, H, KVH, D, bs, dtype, nb_extra=8, seed=0):
@@ -187,8 +183,7 @@ def test_single_long_sequence_splits(built_lib):
 
 def test_many_short_sequences(built_lib):
     batch = _custom_batch([1 + (i % 7) for i in range(2000)], 16, 2, 128, 16, "float16")
-    out = _attend(batch)
-    check_attention(batch, out, seqs=list(range(0, 2000, 97)))
+    check_attention(batch, _attend(batch))
 
 
 def test_workspace_reuse_across_growing_batches(built_lib):
@@ -196,8 +191,7 @@ def test_workspace_reuse_across_growing_batches(built_lib):
     arrival counters; the op must re-zero that prefix before the larger call."""
     for S in (1, 3, 40, 600, 5, 1200):
         batch = _custom_batch([700 + 37 * i for i in range(S)], 14, 2, 64, 16, "bfloat16")
-        out = _attend(batch)
-        check_attention(batch, out, seqs=sorted({0, S // 2, S - 1}))
+        check_attention(batch, _attend(batch))
 
 
 def test_two_streams_use_separate_workspaces(built_lib):

@@ -38,6 +38,7 @@ _PROTOS = {
     "tlb_last_error": [],
     "tlb_version": [],
     "tlb_get_device_status": [ctypes.POINTER(ctypes.c_uint32), _i32, _vp],
+    "tlb_attention_set_wait_limit": [ctypes.c_uint32],
     "tlb_paged_attention_workspace_size": [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_sz)],
     "tlb_paged_attention_workspace_zeroed_bytes": [_i64, _i64, ctypes.POINTER(_sz)],
     "tlb_paged_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
@@ -135,6 +136,7 @@ class device_guard:
         return False
 
 
+STATUS_WAIT_TIMEOUT = 0x10
 STATUS_BITS = {
     0x1: "block id outside the KV pool",
     0x2: "seq_len larger than max_blocks_per_seq * block_size",
@@ -142,6 +144,14 @@ STATUS_BITS = {
     0x8: "slot or logical block outside the cache",
     0x10: "a bounded pipeline wait timed out",
 }
+
+def set_wait_limit(tries: int) -> None:
+    """Probes before a pipeline wait of the attention kernels gives up
+    (failure injection for tests; TLB_WAIT_LIMIT_DEFAULT restores)."""
+    check(load().tlb_attention_set_wait_limit(int(tries)))
+
+
+WAIT_LIMIT_DEFAULT = 1 << 22
 
 # With TLB_DEBUG=1 every op synchronises and raises on a non-zero device
 # status word (bounds problems the kernels skipped instead of faulting).
@@ -155,6 +165,12 @@ def device_status(clear: bool = True, raise_on_error: bool = False) -> int:
     rc = load().tlb_get_device_status(ctypes.byref(v), 1 if clear else 0, stream_of(dev))
     if rc != TLB_OK:
         raise RuntimeError(last_error())
+    if v.value & STATUS_WAIT_TIMEOUT:
+        # A kernel that gave up a wait may have left arrival counters set in
+        # the attention workspaces of this device: zero them before reuse.
+        from . import attention
+
+        attention.invalidate_workspaces(dev.index)
     if raise_on_error and v.value:
         names = [m for b, m in STATUS_BITS.items() if v.value & b]
         raise RuntimeError("tinyllama_b200 device status: " + "; ".join(names))

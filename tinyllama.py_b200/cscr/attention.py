@@ -40,6 +40,15 @@ _workspaces: dict[tuple[int, int], _Workspace] = {}
 _ws_sizes: dict[tuple, tuple[int, int]] = {}
 
 
+def invalidate_workspaces(device_index: int) -> None:
+    """Forget which counter prefixes of this device's workspaces are zero, so
+    that the next call on each re-zeroes its prefix (after a kernel reported
+    a wait that gave up, TLB_STATUS_WAIT_TIMEOUT)."""
+    for (dev, _stream), ws in _workspaces.items():
+        if dev == device_index:
+            ws.clean = 0
+
+
 def workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
                     dtype: torch.dtype, device_index: int) -> tuple[int, int]:
     """(total bytes, zero-at-rest prefix bytes) of scratch for this shape on this device."""

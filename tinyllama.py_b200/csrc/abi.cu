@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -22,6 +23,9 @@ __device__ unsigned int g_status = 0;
 namespace {
 
 thread_local std::string g_last_error;
+// Probes before a pipeline wait of the attention kernels gives up
+// (tlb_attention_set_wait_limit).
+std::atomic<uint32_t> g_wait_limit{TLB_WAIT_LIMIT_DEFAULT};
 
 int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -161,6 +165,11 @@ const char* tlb_last_error(void) { return g_last_error.c_str(); }
 
 const char* tlb_version(void) { return "tinyllama_b200 0.1.0 (sm_100a)"; }
 
+int tlb_attention_set_wait_limit(uint32_t tries) {
+    g_wait_limit.store(tries, std::memory_order_relaxed);
+    return TLB_OK;
+}
+
 int tlb_get_device_status(uint32_t* status_out, int clear, void* stream) {
     TLB_REQUIRE(status_out != nullptr, "status_out must not be null");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -174,6 +183,13 @@ int tlb_get_device_status(uint32_t* status_out, int clear, void* stream) {
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_fail(e, "reading the device status word");
+    if (v & TLB_STATUS_WAIT_TIMEOUT) {
+        // A kernel that gave up a wait may have left arrival counters set in
+        // its scratch: the library's own static scratch is cleared again
+        // before its next use (caller-owned workspaces are the caller's).
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) tlb::no_alloc_scratch_dirty(dev);
+    }
     *status_out = v;
     return TLB_OK;
 }
@@ -218,13 +234,23 @@ struct FusedRope {
     int64_t key_stride, value_stride;
 };
 
-int attention_impl(void* out, const void* query, const void* key_cache,
-                   const void* value_cache, const int32_t* block_tables,
-                   const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
-                   int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
-                   int64_t block_size, int64_t max_blocks_per_seq, float scale, int dtype,
-                   void* workspace, size_t workspace_bytes, unsigned flags, void* stream,
-                   const FusedRope* fr) {
+// Argument checks and path choice of a paged-attention call, before any
+// launch. `ws` gets the workspace layout of the tensor-core path (all zero when
+// the generic kernel serves the call: it uses no workspace).
+struct AttnPlan {
+    bool tc = false;
+    int grid = 0;
+    int gpad = 0;
+    int group = 0;
+    uint64_t rows = 0;
+    WsLayout ws{};
+};
+
+int plan_attention(const void* out, const void* query, const void* key_cache,
+                   const void* value_cache, const int32_t* block_tables, const int32_t* seq_lens,
+                   int64_t num_seqs, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                   int64_t num_blocks, int64_t block_size, int64_t max_blocks_per_seq, int dtype,
+                   unsigned flags, AttnPlan* pl) {
     TLB_REQUIRE(is_float(dtype), "dtype must be float16, bfloat16 or float32");
     TLB_REQUIRE((flags & ~TLB_ATTN_OVERLAP_PROLOGUE) == 0, "unknown flags");
     TLB_REQUIRE(num_seqs > 0, "query must contain at least one sequence");
@@ -241,14 +267,40 @@ int attention_impl(void* out, const void* query, const void* key_cache,
     TLB_REQUIRE(aligned(query, esz) && aligned(out, esz) && aligned(key_cache, esz) &&
                     aligned(value_cache, esz),
                 "tensor pointers must be aligned to the element size");
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int group = (int)(num_heads / num_kv_heads);
-    const float scale_log2 = scale * 1.4426950408889634f;
+    pl->group = (int)(num_heads / num_kv_heads);
+    pl->rows = (uint64_t)num_blocks * num_kv_heads * block_size;
+    pl->tc = tlb::attn::tc_supported(dtype, (int)head_dim, pl->group, (int)block_size) &&
+             aligned(query, 16) && aligned(key_cache, 16) && aligned(value_cache, 16) &&
+             pl->rows < (1ull << 31);
+    pl->ws = WsLayout{};
+    if (!pl->tc) return TLB_OK;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    cudaError_t e;
+    pl->grid = tlb::attn::tc_grid(dev, dtype, (int)head_dim, pl->group, &e);
+    if (pl->grid <= 0) return cuda_fail(e, "sizing the attention grid");
+    pl->gpad = tlb::attn::tc_gpad(pl->group);
+    pl->ws = ws_layout(num_seqs, num_kv_heads, head_dim, pl->gpad, pl->grid);
+    return TLB_OK;
+}
 
-    const uint64_t rows = (uint64_t)num_blocks * num_kv_heads * block_size;
-    const bool tc = tlb::attn::tc_supported(dtype, (int)head_dim, group, (int)block_size) &&
-                    aligned(query, 16) && aligned(key_cache, 16) && aligned(value_cache, 16) &&
-                    rows < (1ull << 31);
+int attention_impl(void* out, const void* query, const void* key_cache,
+                   const void* value_cache, const int32_t* block_tables,
+                   const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
+                   int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                   int64_t block_size, int64_t max_blocks_per_seq, float scale, int dtype,
+                   void* workspace, size_t workspace_bytes, unsigned flags, void* stream,
+                   const FusedRope* fr) {
+    AttnPlan pl;
+    if (int rc = plan_attention(out, query, key_cache, value_cache, block_tables, seq_lens,
+                                num_seqs, num_heads, num_kv_heads, head_dim, num_blocks,
+                                block_size, max_blocks_per_seq, dtype, flags, &pl))
+        return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int group = pl.group;
+    const float scale_log2 = scale * 1.4426950408889634f;
+    const uint64_t rows = pl.rows;
+    const bool tc = pl.tc;
     if (fr != nullptr && !(tc && aligned(fr->cos_sin, 16) && aligned(fr->key, 16) &&
                            aligned(fr->value, 16) && fr->key_stride % 8 == 0 &&
                            fr->value_stride % 8 == 0))
@@ -256,13 +308,9 @@ int attention_impl(void* out, const void* query, const void* key_cache,
                     "the fused decode step needs the tensor-core path (fp16/bf16, head_dim 64 "
                     "or 128, group <= 16, block_size 8..64, 16-byte aligned tensors)");
     if (tc) {
-        int dev;
-        if (int rc = current_device(&dev)) return rc;
         cudaError_t e;
-        const int grid = tlb::attn::tc_grid(dev, dtype, (int)head_dim, group, &e);
-        if (grid <= 0) return cuda_fail(e, "sizing the attention grid");
-        const int gpad = tlb::attn::tc_gpad(group);
-        const WsLayout w = ws_layout(num_seqs, num_kv_heads, head_dim, gpad, grid);
+        const int grid = pl.grid;
+        const WsLayout& w = pl.ws;
         if (workspace == nullptr || workspace_bytes < w.total || !aligned(workspace, 256))
             return fail(TLB_ERR_WORKSPACE,
                         "paged_attention needs a 256-byte aligned workspace of %zu bytes (got %zu)",
@@ -289,6 +337,7 @@ int attention_impl(void* out, const void* query, const void* key_cache,
         p.max_blocks = (int)max_blocks_per_seq;
         p.min_tokens = TLB_ATTN_MIN_TOKENS;
         p.scale_log2 = scale_log2;
+        p.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
         if (fr != nullptr) {
             p.cos_sin = fr->cos_sin;
             p.cache_rows = fr->cache_rows;
@@ -325,6 +374,26 @@ int attention_impl(void* out, const void* query, const void* key_cache,
     return TLB_OK;
 }
 }  // namespace
+
+}  // extern "C"
+
+int tlb::attention_workspace_plan(const void* out, const void* query, const void* key_cache,
+                                  const void* value_cache, const int32_t* block_tables,
+                                  const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
+                                  int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                                  int64_t block_size, int64_t max_blocks_per_seq, int dtype,
+                                  unsigned flags, size_t* total, size_t* zeroed) {
+    AttnPlan pl;
+    if (int rc = plan_attention(out, query, key_cache, value_cache, block_tables, seq_lens,
+                                num_seqs, num_heads, num_kv_heads, head_dim, num_blocks,
+                                block_size, max_blocks_per_seq, dtype, flags, &pl))
+        return rc;
+    *total = pl.ws.total;
+    *zeroed = pl.ws.zeroed;
+    return TLB_OK;
+}
+
+extern "C" {
 
 int tlb_paged_attention(void* out, const void* query, const void* key_cache,
                         const void* value_cache, const int32_t* block_tables,

@@ -174,8 +174,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // hardware-defined interval, so this limit is far above any legitimate wait
 // (a few microseconds) while still ending a wait that would never complete.
 constexpr uint32_t kWaitLimit = 1u << 22;
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+static_assert(kWaitLimit == TLB_WAIT_LIMIT_DEFAULT, "one default bound");
+// `limit` probes at most (0: give up at once without probing).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
     }
     return false;

@@ -10,6 +10,22 @@ namespace tlb {
 // Message returned by tlb_last_error() on this thread (defined in abi.cu).
 void set_last_error(const char* msg);
 
+// The argument checks and path choice of tlb_paged_attention, without
+// launching (abi.cu). On TLB_OK, `total` is the workspace the call will use
+// and `zeroed` the prefix that must be zero when it starts; both are 0 when
+// the kernel that serves the call needs no workspace. No CUDA call beyond
+// device and occupancy queries.
+int attention_workspace_plan(const void* out, const void* query, const void* key_cache,
+                             const void* value_cache, const int32_t* block_tables,
+                             const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
+                             int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                             int64_t block_size, int64_t max_blocks_per_seq, int dtype,
+                             unsigned flags, size_t* total, size_t* zeroed);
+
+// Marks the allocation-free entry point's static scratch on `dev` as not
+// known to be zero (static_scratch.cu), so its next call clears it.
+void no_alloc_scratch_dirty(int dev);
+
 // ------------------------------------------------------------ attention
 namespace attn {
 
@@ -51,6 +67,7 @@ struct TcParams {
     int max_blocks;
     int min_tokens;           // fewest tokens (per kv head) a CTA is given before more join
     float scale_log2;         // softmax scale * log2(e)
+    unsigned wait_limit;      // mbarrier probes before a pipeline wait gives up
     // Fused decode step (cos_sin != nullptr): the new token of sequence s sits
     // at position seq_lens[s] - 1. `query` is then the raw query, rotated in
     // the kernel (NeoX, rot_dim == head_dim); the CTA that reads a sequence's

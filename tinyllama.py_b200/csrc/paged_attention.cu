@@ -246,6 +246,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     constexpr int kCS = kCostStage * ROWS / 64;  // cost of one stage of ROWS tokens
     constexpr int GP = L::kGP;
     constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
+    // probes before a pipeline wait gives up (copy drains keep the default)
+    const uint32_t wlim = p.wait_limit;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -761,7 +763,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             if (!job.valid) break;
 
             bool waited = true;
-            if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
+            if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, wlim);
             waited = __shfl_sync(0xffffffffu, waited, 0);
             if (!waited) {
                 if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
@@ -802,9 +804,10 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                 atomicExch(p.sched + 1, 0u);
             }
         }
+        bool drain = !ok;
         if (ok) {
             bool waited = true;
-            if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1);
+            if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, wlim);
             waited = __shfl_sync(0xffffffffu, waited, 0);
             if (lane == 0) {
                 if (waited) {
@@ -814,10 +817,13 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                     flag_status(TLB_STATUS_WAIT_TIMEOUT);
                 }
             }
-        } else {
+            drain = !waited;
+        }
+        if (drain) {
             // A wait gave up: let the copies already issued land before the
-            // CTA's shared memory is released. Stage `stage` was not issued;
-            // the NSTAGE-1 before it may have been.
+            // CTA's shared memory is released (these waits keep the default
+            // bound: an issued copy always lands). Stage `stage` was not
+            // issued; the NSTAGE-1 before it may have been.
             if (lane == 0) {
                 int st = stage;
                 uint32_t ph = phase;
@@ -839,7 +845,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         constexpr int kPer4 = GP * D / 128;  // float4 groups of the piece per lane
         uint32_t ephase = 0;
         while (true) {
-            if (!mbar_wait_bounded(bar_epi_full, ephase)) {
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar_epi_full, ephase, wlim))) {
                 if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
                 break;
             }
@@ -1128,7 +1134,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     uint32_t cphase = 0;
     auto csync = [&]() -> bool {
         mbar_arrive(bar_cons);
-        const bool ok = mbar_wait_bounded(bar_cons, cphase);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_cons, cphase, wlim));
         cphase ^= 1;
         if (!ok && lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
         return ok;
@@ -1291,7 +1297,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
 
     while (true) {
         bool got = true;
-        got = mbar_wait_bounded(bar_full + 8 * stage, phase);
+        // warp-uniform outcome: the warp's mma and shuffles below need all lanes
+        got = __all_sync(0xffffffffu, mbar_wait_bounded(bar_full + 8 * stage, phase, wlim));
         if (!got) {
             if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
             break;
@@ -1509,7 +1516,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             v += __shfl_xor_sync(0xffffffffu, v, 2);
             lsum[hh] = v;
         }
-        if (!mbar_wait_bounded(bar_epi_empty, ephase ^ 1)) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar_epi_empty, ephase ^ 1, wlim))) {
             if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
             break;
         }
@@ -1543,7 +1550,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         ephase ^= 1;
     }
     // Let the epilogue warp finish once it has taken the last piece.
-    if (mbar_wait_bounded(bar_epi_empty, ephase ^ 1)) {
+    if (__all_sync(0xffffffffu, mbar_wait_bounded(bar_epi_empty, ephase ^ 1, wlim))) {
         if (tid == 0) sEpi->flags = kTerminate;
         mbar_arrive(bar_epi_full);
     } else if (lane == 0) {

@@ -45,32 +45,47 @@ int set_error(int code, const char* msg) {
 
 }  // namespace
 
+// Forget which prefix of the array is zero on `dev`: the next call clears it.
+// Called when a launch failed or a bounded wait inside a kernel gave up (a
+// kernel that stopped early may leave arrival counters set).
+void tlb::no_alloc_scratch_dirty(int dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (dev >= 0 && dev < 64) g_dev[dev].clean = 0;
+}
+
 extern "C" int tlb_paged_attention_no_alloc(
     void* out, const void* query, const void* key_cache, const void* value_cache,
     const int32_t* block_tables, const int32_t* seq_lens, int64_t num_seqs, int64_t num_heads,
     int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
     int64_t max_blocks_per_seq, float scale, int dtype, unsigned flags, void* stream) {
+    // Every argument check of tlb_paged_attention first, and the scratch this
+    // call will really use (none when the kernel serving it needs none).
     size_t need = 0, zeroed = 0;
-    if (num_seqs > 0 && num_heads > 0 && num_kv_heads > 0 && head_dim > 0 &&
-        num_heads % num_kv_heads == 0) {
-        if (int rc = tlb_paged_attention_workspace_size(num_seqs, num_heads, num_kv_heads,
-                                                        head_dim, dtype, &need))
-            return rc;
-        if (int rc = tlb_paged_attention_workspace_zeroed_bytes(num_seqs, num_kv_heads, &zeroed))
-            return rc;
-        if (need > kNoAllocScratchBytes) {
-            char buf[200];
-            snprintf(buf, sizeof(buf),
-                     "paged_attention_no_alloc: this batch needs %zu bytes of scratch, more than "
-                     "the %zu-byte static buffer (fewer sequences per call fit)",
-                     need, kNoAllocScratchBytes);
-            return set_error(TLB_ERR_WORKSPACE, buf);
-        }
+    if (int rc = tlb::attention_workspace_plan(out, query, key_cache, value_cache, block_tables,
+                                               seq_lens, num_seqs, num_heads, num_kv_heads,
+                                               head_dim, num_blocks, block_size,
+                                               max_blocks_per_seq, dtype, flags, &need, &zeroed))
+        return rc;
+    if (need > kNoAllocScratchBytes || zeroed > kNoAllocScratchBytes) {
+        char buf[200];
+        snprintf(buf, sizeof(buf),
+                 "paged_attention_no_alloc: this batch needs %zu bytes of scratch, more than "
+                 "the %zu-byte static buffer (fewer sequences per call fit)",
+                 need > zeroed ? need : zeroed, kNoAllocScratchBytes);
+        return set_error(TLB_ERR_WORKSPACE, buf);
     }
+    if (need == 0)  // served by the kernel that uses no scratch: nothing to set up
+        return tlb_paged_attention(out, query, key_cache, value_cache, block_tables, seq_lens,
+                                   num_seqs, num_heads, num_kv_heads, head_dim, num_blocks,
+                                   block_size, max_blocks_per_seq, scale, dtype, nullptr, 0,
+                                   flags, stream);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return set_error(TLB_ERR_CUDA, "paged_attention_no_alloc: no current CUDA device");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &capturing) != cudaSuccess)
+        return set_error(TLB_ERR_CUDA, "paged_attention_no_alloc: cudaStreamIsCapturing failed");
     void* scratch = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
@@ -87,9 +102,11 @@ extern "C" int tlb_paged_attention_no_alloc(
             d.clean = 0;
         }
         // The kernel needs its counter prefix zero and leaves it zero; a call
-        // with a longer prefix than any clean one clears it first (a memset on
-        // the same stream, no allocation).
-        if (zeroed > d.clean) {
+        // with a longer prefix than the clean one clears it first (a memset
+        // on the same stream, no allocation). A call recorded into a stream
+        // capture always clears it: the host cannot know what ran on the
+        // device between the capture and a later replay.
+        if (zeroed > d.clean || capturing != cudaStreamCaptureStatusNone) {
             if (cudaMemsetAsync(d.ptr, 0, zeroed, st) != cudaSuccess)
                 return set_error(TLB_ERR_CUDA, "paged_attention_no_alloc: clearing scratch failed");
         }
@@ -100,9 +117,6 @@ extern "C" int tlb_paged_attention_no_alloc(
                                        seq_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                                        num_blocks, block_size, max_blocks_per_seq, scale, dtype,
                                        scratch, kNoAllocScratchBytes, flags, stream);
-    if (rc != TLB_OK) {
-        std::lock_guard<std::mutex> lk(g_mu);
-        g_dev[dev].clean = 0;  // state unknown after a failed launch: clear next time
-    }
+    if (rc != TLB_OK) tlb::no_alloc_scratch_dirty(dev);  // state unknown: clear next time
     return rc;
 }
