@@ -335,6 +335,32 @@ TLB_API int tlb_decode_metadata(const int32_t* context_lens,
                         int64_t* positions_out, int64_t* slots_out,
                         void* stream);
 
+/* ------------------------------------------------------------------------
+ * Metadata of a packed continuous-batching step on the device
+ * (src/worker/worker.py:84-169): the tokens of every prompt first, position i
+ * of prompt p at slot prompt_tables[p, i / block_size] * block_size +
+ * i % block_size (:111-124), then one token per decode sequence r at position
+ * context_lens[r] - 1 with its slot as tlb_decode_metadata (:144-159).
+ *   prompt_lens   : [num_prompts] int32 (num_prompts <= 4096)
+ *   prompt_tables : [num_prompts, prompt_max_blocks] int32
+ *   context_lens  : [num_decode] int32; decode_tables [num_decode,
+ *                   decode_max_blocks] int32
+ *   num_tokens    : sum(prompt_lens) + num_decode, the step's packed tokens
+ *   positions_out, slots_out : [round_up(num_tokens, alignment)] int64
+ * Entries past num_tokens hold position 0 (the worker pads its positions with
+ * 0 to a multiple of 8, :163-164) and slot -1 (skipped by the cache writes).
+ * A negative block id, or a position beyond its table, gives slot -1 (the
+ * latter also sets TLB_STATUS_BAD_SLOT). No reference counterpart as a
+ * native op: the worker computes these lists in Python and discards the
+ * slots.
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_step_metadata(const int32_t* prompt_lens, const int32_t* prompt_tables,
+                        int64_t num_prompts, int64_t prompt_max_blocks,
+                        const int32_t* context_lens, const int32_t* decode_tables,
+                        int64_t num_decode, int64_t decode_max_blocks,
+                        int64_t block_size, int64_t num_tokens, int64_t alignment,
+                        int64_t* positions_out, int64_t* slots_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

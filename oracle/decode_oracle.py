@@ -257,6 +257,30 @@ def decode_metadata(context_lens, block_tables, block_size):
     return pos, slots
 
 
+def step_metadata(prompt_lens, prompt_tables, context_lens, decode_tables, block_size,
+                  alignment: int = 8):
+    """positions and slots of a packed continuous-batching step, as
+    worker.py:84-169 forms them: every prompt's tokens first (position i of
+    prompt p at slot prompt_table[p][i // bs] * bs + i % bs, :95-124), then one
+    token per decode sequence (position context_len - 1, slot as
+    decode_metadata, :126-159). Positions are padded with 0 to a multiple of
+    ``alignment`` (:163-164); the slots are returned unpadded, as the worker
+    forms them. A negative block id gives slot -1 (the decode rule here; the
+    reference's block manager never hands out one for a prompt).
+    """
+    pos, slots = [], []
+    for L, table in zip(prompt_lens, prompt_tables):
+        for i in range(int(L)):
+            blk = int(table[i // block_size])
+            pos.append(i)
+            slots.append(blk * block_size + i % block_size if blk >= 0 else -1)
+    dpos, dslots = decode_metadata(context_lens, decode_tables, block_size)
+    pos.extend(int(p) for p in dpos)
+    slots.extend(int(s) for s in dslots)
+    padded = pos + [0] * ((-len(pos)) % alignment)
+    return np.asarray(padded, np.int64), np.asarray(slots, np.int64)
+
+
 # ------------------------------------------------------------ block copies
 def copy_blocks(caches, block_mapping):
     """cscr/cache_kernel.cu:124-212 (copy_blocks): src block -> each dst, every cache."""
@@ -279,6 +303,6 @@ def ceil_div(a, b):
 __all__ = [
     "DTYPES", "bf16_bits_to_f32", "f32_to_bf16_bits", "to_f32", "from_f32", "storage_np_dtype",
     "paged_attention", "paged_attention_f32", "paged_attention_threads", "rotary_embedding_neox", "cos_sin_cache",
-    "write_kv_cache", "reshape_and_cache", "decode_metadata", "copy_blocks", "swap_blocks",
+    "write_kv_cache", "reshape_and_cache", "decode_metadata", "step_metadata", "copy_blocks", "swap_blocks",
     "ceil_div",
 ]

@@ -21,6 +21,10 @@ What each fixture pins, all produced on CPU by the reference's Python:
 * ``decode_meta.npz`` — ``Worker._prepare_inputs`` (src/worker/worker.py:84-169)
   on decode sequence groups; its local ``slot_mappings`` / ``context_lens``
   (computed, then dropped by the reference) are captured with a trace hook.
+* ``step_meta.npz`` — the same on a continuous-batching step that mixes prompt
+  groups and decode groups of one or two sequences: prompt slots (:111-124),
+  decode slots (:144-159) and the positions returned after the pad to a
+  multiple of 8 (:163-169).
 
 The reference imports ``cscr`` at module load; the ``cscr`` package of this
 repository is put first on ``sys.path`` so that import resolves without the
@@ -181,6 +185,80 @@ def gen_decode_meta(ref_root: Path) -> None:
                         block_size=bs, seq_ctx=np.asarray(ctx, np.int32))
 
 
+def gen_step_meta(ref_root: Path) -> None:
+    """``_prepare_inputs`` on a continuous-batching step: prompt groups (their
+    whole prompt, slots from the group's block table, worker.py:95-124) and
+    decode groups of one or two sequences (worker.py:126-159), packed prompt
+    tokens first, then padded to a multiple of 8 (:163-164)."""
+    from src.sampler_params import SamplerParams
+    from src.sequence import SequenceData, SequenceGroupMetadata
+    from src.worker.worker import Worker
+
+    rng = np.random.default_rng(11)
+    bs = 16
+    groups = []
+    prompt_lens, prompt_tables, dec_tables, dec_ctx = [], [], [], []
+    sid = 0
+    kinds = ["p", "d", "d", "p", "d", "p", "d", "d", "d", "p", "d"]
+    for i, kind in enumerate(kinds):
+        if kind == "p":
+            L = int(rng.integers(1, 200))
+            table = rng.permutation(4000)[: -(-L // bs)].tolist()
+            data = SequenceData(prompt_token_ids=rng.integers(1, 1000, L).tolist())
+            groups.append(SequenceGroupMetadata(reqeust_id=str(i), is_prompt=True,
+                                                seq_data={sid: data},
+                                                sampling_params=SamplerParams(),
+                                                block_tables={sid: table}))
+            prompt_lens.append(L)
+            prompt_tables.append(table)
+            sid += 1
+            continue
+        seq_data, tables = {}, {}
+        for _ in range(1 + (i % 2)):  # one or two sequences per decode group
+            P = int(rng.integers(1, 150))
+            data = SequenceData(prompt_token_ids=rng.integers(1, 1000, P).tolist())
+            for _ in range(int(rng.integers(0, 60))):
+                data.append_token_id(int(rng.integers(1, 1000)), 0.0)
+            table = rng.permutation(4000)[: -(-data.get_len() // bs)].tolist()
+            seq_data[sid], tables[sid] = data, table
+            dec_tables.append(table)
+            dec_ctx.append(data.get_len())
+            sid += 1
+        groups.append(SequenceGroupMetadata(reqeust_id=str(i), is_prompt=False,
+                                            seq_data=seq_data, sampling_params=SamplerParams(),
+                                            block_tables=tables))
+    worker = object.__new__(Worker)
+    worker.block_size = bs
+    captured = {}
+
+    def tracer(frame, event, arg):
+        if event == "return" and frame.f_code.co_name == "_prepare_inputs":
+            captured.update({k: list(frame.f_locals[k]) for k in
+                             ("slot_mappings", "context_lens", "input_postions")})
+        return tracer
+
+    sys.settrace(tracer)
+    try:
+        tokens, positions = worker._prepare_inputs(groups)
+    finally:
+        sys.settrace(None)
+
+    def table_array(rows):
+        out = np.full((len(rows), max(len(r) for r in rows)), -1, np.int32)
+        for r, t in enumerate(rows):
+            out[r, : len(t)] = t
+        return out
+
+    np.savez_compressed(HERE / "step_meta.npz", block_size=bs,
+                        prompt_lens=np.asarray(prompt_lens, np.int32),
+                        prompt_tables=table_array(prompt_tables),
+                        context_lens=np.asarray(dec_ctx, np.int32),
+                        decode_tables=table_array(dec_tables),
+                        captured_context_lens=np.asarray(captured["context_lens"], np.int32),
+                        slots=np.asarray(captured["slot_mappings"], np.int64),
+                        positions_padded=_np(positions), num_tokens_padded=len(tokens))
+
+
 def main() -> None:
     ref_root = Path(sys.argv[1]).resolve()
     sys.path.insert(0, str(ref_root))
@@ -190,6 +268,7 @@ def main() -> None:
     gen_cos_sin(ref_root)
     gen_write_kv(ref_root)
     gen_decode_meta(ref_root)
+    gen_step_meta(ref_root)
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -41,7 +41,7 @@ def check_attention(batch: W.DecodeBatch, out: torch.Tensor, seqs=None, query=No
     """Compare `out` ([S, H, D] on device) with the oracle for the given sequences."""
     dtype = batch.spec.dtype
     kc, vc, tables, lens = W.compact_for_oracle(batch) if seqs is None else _subset(batch, seqs)
-    q = W.to_numpy(batch.query[: batch.num_decode] if query is None else query)
+    q = W.to_numpy(batch.query[batch.decode_rows] if query is None else query)
     got = W.to_numpy(out)
     if seqs is not None:
         q, got = q[seqs], got[seqs]

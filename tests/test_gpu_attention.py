@@ -20,7 +20,7 @@ ATTN_CASES = sorted(glob.glob(str(GOLDEN / "attn_ref_test_*.npz")))
 
 
 def _attend(batch, query=None):
-    q = batch.query[: batch.num_decode] if query is None else query
+    q = batch.query[batch.decode_rows] if query is None else query
     return A.paged_attention(q.contiguous(), batch.key_cache, batch.value_cache,
                              batch.block_tables, batch.seq_lens, batch.scale)
 

@@ -108,3 +108,63 @@ def test_paged_attention_with_rope_layer(build, given_positions, built_lib):
     ref = O.paged_attention_f32(q_rot.reshape(S, 16, 128), kc, vc, W.to_numpy(b.block_tables),
                                 W.to_numpy(b.seq_lens), b.scale, "bfloat16")
     np.testing.assert_allclose(O.to_f32(W.to_numpy(out), "bfloat16"), ref, **HALF_TOL)
+
+
+def _device_step(prompt_tables, prompt_lens, decode_tables, context_lens, bs, alignment=8):
+    md = M.step_metadata(prompt_tables, prompt_lens, decode_tables, context_lens, bs,
+                         alignment=alignment)
+    torch.cuda.synchronize()
+    return md.positions.cpu().numpy(), md.slot_mapping.cpu().numpy(), md.num_tokens
+
+
+def test_step_metadata_matches_reference_worker(built_lib):
+    """tlb_step_metadata against _prepare_inputs on a mixed prompt + decode step:
+    prompt slots, decode slots and the positions padded to a multiple of 8."""
+    z = np.load(GOLDEN / "step_meta.npz")
+    pt = [row[row >= 0].tolist() for row in z["prompt_tables"]]
+    dt = [row[row >= 0].tolist() for row in z["decode_tables"]]
+    pos, slots, T = _device_step(pt, z["prompt_lens"].tolist(), dt, z["context_lens"].tolist(),
+                                 int(z["block_size"]))
+    assert np.array_equal(pos, z["positions_padded"])
+    assert T == len(z["slots"])
+    assert np.array_equal(slots[:T], z["slots"])
+    assert np.all(slots[T:] == -1)
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("case", ["decode_only", "prompts_only", "empty_prompt", "negative_block",
+                                  "many_prompts", "alignment_1"])
+def test_step_metadata_edge_cases(case, built_lib):
+    rng = np.random.default_rng(5)
+    bs = 16
+
+    def table(L):
+        return rng.permutation(100_000)[: -(-L // bs)].tolist()
+
+    plens = {"decode_only": [], "prompts_only": [5, 300, 17], "empty_prompt": [4, 0, 9],
+             "negative_block": [40], "many_prompts": rng.integers(0, 50, 3000).tolist(),
+             "alignment_1": [3]}[case]
+    ctx = [] if case == "prompts_only" else [1, 16, 17, 250]
+    ptabs = [table(max(L, 1)) for L in plens]
+    dtabs = [table(L) for L in ctx]
+    if case == "negative_block":
+        ptabs[0][1] = -1
+        dtabs[2][1] = -1
+    align = 1 if case == "alignment_1" else 8
+    pos, slots, T = _device_step(ptabs, plens, dtabs, ctx, bs, alignment=align)
+    ref_pos, ref_slots = O.step_metadata(plens, ptabs, ctx, dtabs, bs, alignment=align)
+    assert np.array_equal(pos, ref_pos)
+    assert np.array_equal(slots[:T], ref_slots)
+    assert np.all(slots[T:] == -1) and len(pos) % align == 0
+    assert _lib.device_status() == 0
+
+
+def test_ragged_step_built_on_device_matches_host(built_lib):
+    """Config 3 (4 prompts + 252 decode sequences): the device-built positions
+    and slot mapping the workload uses equal the host-derived ones."""
+    spec = W.ragged_batch(0)
+    dev = W.make_batch(spec, fill_cache=False)
+    host = W.make_batch(spec, device="cpu", fill_cache=False)
+    assert torch.equal(dev.positions.cpu(), host.positions)
+    assert torch.equal(dev.slot_mapping.cpu(), host.slot_mapping)
+    assert dev.num_prompt_tokens == sum(spec.prefill_lens)

@@ -142,9 +142,8 @@ def _attn_case(name):
         return b.query, b.key_cache, b.value_cache, b.block_tables, b.seq_lens, b.scale, "bfloat16"
     if name == "ragged_batch_decode":
         b = W.make_batch(W.ragged_batch(0))
-        S = b.num_decode
-        return (b.query[:S].contiguous(), b.key_cache, b.value_cache, b.block_tables, b.seq_lens,
-                b.scale, "float16")
+        return (b.query[b.decode_rows].contiguous(), b.key_cache, b.value_cache,
+                b.block_tables, b.seq_lens, b.scale, "float16")
     if name.startswith("hd64"):
         dtype = name.split("_")[-1]
         spec = W.DecodeSpec("hd64", [1, 7, 64, 333, 1024, 2500, 4096, 17], 14, 2, 64, 16, dtype,

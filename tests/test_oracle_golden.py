@@ -70,6 +70,18 @@ def test_write_kv_fixture_skips_negative_blocks():
     assert changed.sum() == len(z["positions"]) - 2
 
 
+def test_step_metadata_oracle():
+    """A prompt + decode step: prompt slots, decode slots and padded positions
+    exactly as the reference's _prepare_inputs formed them."""
+    z = np.load(GOLDEN / "step_meta.npz")
+    pos, slots = O.step_metadata(z["prompt_lens"], z["prompt_tables"], z["context_lens"],
+                                 z["decode_tables"], int(z["block_size"]))
+    assert np.array_equal(pos, z["positions_padded"])
+    assert np.array_equal(slots, z["slots"])
+    assert len(pos) == int(z["num_tokens_padded"]) and len(pos) % 8 == 0
+    assert np.array_equal(z["context_lens"], z["captured_context_lens"])
+
+
 def test_decode_metadata_oracle():
     z = np.load(GOLDEN / "decode_meta.npz")
     pos, slots = O.decode_metadata(z["context_lens"], z["block_tables"], int(z["block_size"]))

@@ -61,6 +61,8 @@ _PROTOS = {
     "tlb_copy_blocks": [ctypes.POINTER(_vp), _i64, ctypes.POINTER(_i64), _i64, _i64, _vp],
     "tlb_swap_blocks": [_vp, _i32, _vp, _i32, ctypes.POINTER(_i64), _i64, _i64, _vp],
     "tlb_decode_metadata": [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp],
+    "tlb_step_metadata": [_vp, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
+                          _vp],
 }
 _RESTYPES = {"tlb_last_error": ctypes.c_char_p, "tlb_version": ctypes.c_char_p}
 

@@ -651,6 +651,35 @@ int tlb_decode_metadata(const int32_t* context_lens, const int32_t* block_tables
     return TLB_OK;
 }
 
+int tlb_step_metadata(const int32_t* prompt_lens, const int32_t* prompt_tables,
+                      int64_t num_prompts, int64_t prompt_max_blocks,
+                      const int32_t* context_lens, const int32_t* decode_tables,
+                      int64_t num_decode, int64_t decode_max_blocks, int64_t block_size,
+                      int64_t num_tokens, int64_t alignment, int64_t* positions_out,
+                      int64_t* slots_out, void* stream) {
+    TLB_REQUIRE(num_prompts >= 0 && num_decode >= 0 && num_tokens >= 0,
+                "counts must not be negative");
+    TLB_REQUIRE(num_prompts <= tlb::kStepMaxPrompts, "at most %d prompts per step",
+                tlb::kStepMaxPrompts);
+    TLB_REQUIRE(block_size > 0 && alignment > 0, "block_size and alignment must be positive");
+    TLB_REQUIRE(num_prompts == 0 || (prompt_lens && prompt_tables && prompt_max_blocks > 0),
+                "prompt_lens and prompt_tables are required when there are prompts");
+    TLB_REQUIRE(num_decode == 0 || (context_lens && decode_tables && decode_max_blocks > 0),
+                "context_lens and decode_tables are required when there are decode sequences");
+    TLB_REQUIRE(num_tokens >= num_decode, "num_tokens must count every decode token");
+    TLB_REQUIRE(prompt_max_blocks < (1ll << 31) && decode_max_blocks < (1ll << 31) &&
+                    block_size < (1ll << 31),
+                "sizes exceed the supported range");
+    const int64_t padded = (num_tokens + alignment - 1) / alignment * alignment;
+    TLB_REQUIRE(padded == 0 || (positions_out && slots_out), "output pointers must not be null");
+    cudaError_t e = tlb::launch_step_metadata(
+        prompt_lens, prompt_tables, (int)num_prompts, (int)prompt_max_blocks, context_lens,
+        decode_tables, num_decode, (int)decode_max_blocks, (int)block_size, padded,
+        positions_out, slots_out, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "launching step_metadata");
+    return TLB_OK;
+}
+
 // ------------------------------------------------------------ block copies
 int tlb_copy_blocks(void* const* caches, int64_t num_caches, const int64_t* pairs,
                     int64_t num_pairs, int64_t block_bytes, void* stream) {

@@ -156,6 +156,16 @@ cudaError_t launch_decode_metadata(const int32_t* context_lens, const int32_t* b
                                    long long num_seqs, int max_blocks, int block_size,
                                    int64_t* positions, int64_t* slots, cudaStream_t stream);
 
+// Positions and slots of a packed step: prompts' tokens, then one token per
+// decode sequence, padded to `num_padded` entries (step_metadata.cu).
+constexpr int kStepMaxPrompts = 4096;
+cudaError_t launch_step_metadata(const int32_t* prompt_lens, const int32_t* prompt_tables,
+                                 int num_prompts, int prompt_max_blocks,
+                                 const int32_t* context_lens, const int32_t* decode_tables,
+                                 long long num_decode, int decode_max_blocks, int block_size,
+                                 long long num_padded, int64_t* positions, int64_t* slots,
+                                 cudaStream_t stream);
+
 // ------------------------------------------------------------ block copies
 constexpr int kCopyMaxCaches = 128;
 constexpr int kCopyMaxPairs = 1024;

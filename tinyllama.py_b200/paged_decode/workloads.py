@@ -6,7 +6,7 @@ are N(0, 1) from a seeded torch generator, and physical blocks are a seeded
 random permutation of the pool. Each workload is a decode step: one new token
 per sequence at position ``context_len - 1`` whose slot lies in the
 sequence's last block, plus, for the continuous-batching shape, prefill
-chunks that only take part in RoPE and the cache write.
+chunks packed before the decode tokens as the reference's worker packs them.
 
 Shapes (H query heads / KVH kv heads / D head dim, bs block size):
   uniform_small   8 seqs, len U[1,512], H16/KVH2/D128, bs16, 512 blocks, fp32
@@ -136,7 +136,7 @@ def cos_sin_table(rotary_dim: int, max_position: int, base: float, dtype: torch.
 class DecodeBatch:
     """Device (or host) tensors of one decode step."""
     spec: DecodeSpec
-    query: torch.Tensor          # [T, H, D]   new tokens (decode tokens first)
+    query: torch.Tensor          # [T, H, D]   new tokens (prefill tokens, then decode)
     key: torch.Tensor            # [T, KVH, D]
     value: torch.Tensor          # [T, KVH, D]
     positions: torch.Tensor      # [T] int64
@@ -148,10 +148,16 @@ class DecodeBatch:
     value_cache: torch.Tensor
     cos_sin_cache: torch.Tensor  # [max_position, D]
     scale: float
+    num_prompt_tokens: int = 0   # prefill tokens packed before the decode tokens
 
     @property
     def num_decode(self) -> int:
         return self.block_tables.shape[0]
+
+    @property
+    def decode_rows(self) -> slice:
+        """Rows of query / key / value holding the decode tokens."""
+        return slice(self.num_prompt_tokens, self.num_prompt_tokens + self.num_decode)
 
 
 def make_batch(spec: DecodeSpec, device="cuda", fill_cache: bool = True,
@@ -182,16 +188,11 @@ def make_batch(spec: DecodeSpec, device="cuda", fill_cache: bool = True,
         pre_tables.append(perm[off:off + n])
         off += n
 
-    # new tokens: one per decode sequence, then every prefill chunk token
+    # new tokens packed as the reference's worker packs them
+    # (src/worker/worker.py:95-159): every prefill chunk's tokens, then one
+    # per decode sequence
     pos, slots, tok_rows = [], [], []
     maxB_all = max([maxB] + nb_pre)
-    for s, L in enumerate(dec_lens):
-        p = L - 1
-        pos.append(p)
-        slots.append(int(tables[s, p // bs]) * bs + p % bs if p >= 0 else -1)
-        row = np.zeros(maxB_all, np.int32)
-        row[:maxB] = tables[s]
-        tok_rows.append(row)
     for c, L in enumerate(spec.prefill_lens):
         row = np.zeros(maxB_all, np.int32)
         row[:len(pre_tables[c])] = pre_tables[c]
@@ -199,7 +200,15 @@ def make_batch(spec: DecodeSpec, device="cuda", fill_cache: bool = True,
             pos.append(p)
             slots.append(int(pre_tables[c][p // bs]) * bs + p % bs)
             tok_rows.append(row)
+    for s, L in enumerate(dec_lens):
+        p = L - 1
+        pos.append(p)
+        slots.append(int(tables[s, p // bs]) * bs + p % bs if p >= 0 else -1)
+        row = np.zeros(maxB_all, np.int32)
+        row[:maxB] = tables[s]
+        tok_rows.append(row)
     T = len(pos)
+    n_prompt = T - S
 
     g = torch.Generator(device="cpu").manual_seed(spec.seed)
     gen_dev = torch.Generator(device=dev).manual_seed(spec.seed) if dev.type == "cuda" else g
@@ -222,14 +231,25 @@ def make_batch(spec: DecodeSpec, device="cuda", fill_cache: bool = True,
     max_pos = spec.max_position or max([1] + dec_lens + list(spec.prefill_lens))
     cs = cos_sin_table(D, max_pos, spec.rope_theta, dtype,
                        build_dtype if build_dtype is not None else torch.float32).to(dev)
+    positions = torch.tensor(pos, dtype=torch.int64, device=dev)
+    slot_mapping = torch.tensor(slots, dtype=torch.int64, device=dev)
+    if spec.prefill_lens and dev.type == "cuda":
+        # A step with prompts: positions and slots come from the device-side
+        # builder, from the block tables and lengths the block manager holds.
+        from paged_decode import metadata as M
+
+        md = M.step_metadata([t.tolist() for t in pre_tables], list(spec.prefill_lens),
+                             [tables[s, :nb_dec[s]].tolist() for s in range(S)], dec_lens, bs,
+                             device=dev)
+        positions, slot_mapping = md.positions[:T], md.slot_mapping[:T]
     return DecodeBatch(
         spec=spec, query=query, key=key, value=value,
-        positions=torch.tensor(pos, dtype=torch.int64, device=dev),
-        slot_mapping=torch.tensor(slots, dtype=torch.int64, device=dev),
+        positions=positions, slot_mapping=slot_mapping,
         token_block_tables=torch.from_numpy(np.stack(tok_rows)).to(dev),
         block_tables=torch.from_numpy(tables).to(dev),
         seq_lens=torch.tensor(dec_lens, dtype=torch.int32, device=dev),
-        key_cache=kc, value_cache=vc, cos_sin_cache=cs, scale=D ** -0.5)
+        key_cache=kc, value_cache=vc, cos_sin_cache=cs, scale=D ** -0.5,
+        num_prompt_tokens=n_prompt)
 
 
 def to_numpy(t: torch.Tensor) -> np.ndarray:
