@@ -67,6 +67,13 @@ def parse():
                          "(rounded to a multiple of --layers; 4 measured best of 4, 8, 12)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="rotating independent KV pools per GPU (profiling runs use 1)")
+    ap.add_argument("--workload", choices=["qwen3b", "long_tail", "ragged"], default="qwen3b",
+                    help="qwen3b: the decode step (default); long_tail: 256 long-tailed "
+                         "sequences LPT-split over the GPUs, ~150 GB pool each (strong "
+                         "scaling); ragged: decode + prompt chunks with prefill attention, "
+                         "1 GPU")
+    ap.add_argument("--pool-gb", type=float, default=150.0,
+                    help="long_tail: KV pool per GPU in GB")
     ap.add_argument("--sweep", action="store_true",
                     help="shape sweep (block size x batch x context x dtype x heads): one JSON "
                          "line per point with the attention kernel's rate and the CPU oracle's")
@@ -197,6 +204,17 @@ def measured_hbm_peak():
         except (ValueError, KeyError):
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16 tensor peak (TFLOP/s) measured on this pool, burst figure."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return 1590.0, "fallback"
 
 
 def profiled_traffic(key: str):
@@ -624,6 +642,254 @@ def run_e2e_eager(args, layers, dev, world, barrier):
                     "of its output on the same stream"}
 
 
+# -------------------------------------------------- long-tail (config 4)
+LONG_TAIL = ("long-tail decode step: 256 seqs in all, ctx clip(32*(1+pareto(1.2)), 32, 32768), "
+             "16q/2kv heads, hd128, bs32, bf16, ~150 GB pool per GPU")
+
+
+def _timed_graph(graph, stream, dev, reps, warm, world, barrier):
+    """Device time of `reps` replays after `warm` untimed ones: (max over
+    ranks, this rank's own)."""
+    import torch.distributed as dist
+
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            graph.replay()
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    own = e0.elapsed_time(e1)
+    ms = own
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return ms, own
+
+
+def run_long_tail(args, rank, world, local):
+    """Config 4: one global batch of 256 long-tailed sequences, LPT-split over
+    the GPUs (strong scaling), each GPU with a ~150 GB block pool; per step the
+    fused decode step of every sequence (RoPE + cache write + attention).
+    Steps rotate over 4 disjoint block sets of the pool (> 126 MB of KV per
+    rotation), so no step finds its KV in L2."""
+    import torch.distributed as dist
+
+    from cscr import attention as A
+    from paged_decode import partition as Pn
+    from paged_decode import pool as Pool
+    from paged_decode import roofline as R
+    from paged_decode import workloads as W
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=300))
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    lens = W.long_tail_lengths(args.seed, batch=256)
+    shards = Pn.lpt_assign(lens, world)
+    mine = [lens[i] for i in shards[rank]]
+    H, KVH, D, bs = 16, 2, 128, 32
+    budget = int(args.pool_gb * 1e9)
+    NB = Pool.blocks_for_budget(budget, 1, KVH, D, bs, torch.bfloat16)
+    (kc, vc), = Pool.allocate_kv_cache(1, NB, KVH, D, bs, torch.bfloat16, device=dev)
+    nl = args.layers
+    layers = [W.make_batch(W.DecodeSpec("long_tail", mine, H, KVH, D, bs, "bfloat16",
+                                        num_blocks=NB, max_position=32768,
+                                        seed=args.seed * 1000 + rank * 10 + l),
+                           device=dev, caches=(kc, vc)) for l in range(nl)]
+    S = len(mine)
+    stream = torch.cuda.Stream(dev)
+
+    def step(b):
+        return A.paged_attention_with_rope(b.query, b.key.view(S, KVH * D), b.value,
+                                           b.key_cache, b.value_cache, b.block_tables,
+                                           b.seq_lens, b.cos_sin_cache, b.scale,
+                                           overlap_prologue=True)
+
+    with torch.cuda.stream(stream):
+        for b in layers:
+            step(b)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for b in layers:
+                step(b)
+    reps = max(1, args.steps // nl)
+    steps = reps * nl
+    ms, own = _timed_graph(g, stream, dev, reps, max(1, math.ceil(args.warmup / nl)), world,
+                           barrier)
+    per_step_bytes = statistics.fmean(
+        R.attention_bytes(b.seq_lens.cpu().numpy(), bs, H, KVH, D, 2) for b in layers) + \
+        R.rope_bytes(S, H, KVH, D, D, 2) + R.cache_write_bytes(S, KVH, D, 2)
+    mine_t = torch.tensor([own * 1e3 / steps, per_step_bytes, float(sum(mine)), float(S)],
+                          dtype=torch.float64, device=dev)
+    if world > 1:
+        gathered = [torch.empty_like(mine_t) for _ in range(world)]
+        dist.all_gather(gathered, mine_t)
+    else:
+        gathered = [mine_t]
+    del g
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    per_rank = [{"rank": r, "seqs": int(x[3]), "context_tokens": int(x[2]),
+                 "us_per_step": round(float(x[0]), 3), "bytes_per_step": int(x[1]),
+                 "gbs": round(float(x[1]) / (float(x[0]) * 1e-6) / 1e9, 1)}
+                for r, x in enumerate(t.cpu() for t in gathered)]
+    peak, peak_kind = measured_hbm_peak()
+    total_bytes = sum(pr["bytes_per_step"] for pr in per_rank)
+    t_step = ms * 1e3 / steps
+    bound_tokens = Pn.makespan_bound(lens, world)
+    return {
+        "metric": METRIC, "value": round(256 * steps / (ms / 1e3), 1), "unit": UNIT,
+        "n_gpus": world, "steps": steps, "warmup": max(1, math.ceil(args.warmup / nl)) * nl,
+        "ms_per_step": round(ms / steps, 6), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v and KV blocks, seeded Pareto lengths)",
+        "config": {"workload": LONG_TAIL, "global_batch": 256, "seq_len": "Pareto(1.2) x 32, "
+                   "clipped to [32, 32768]", "parallelism": f"sequence-sharded x{world} (LPT), "
+                   "no collective", "pool_blocks_per_gpu": NB,
+                   "pool_gb_per_gpu": round(2 * NB * KVH * bs * D * 2 / 1e9, 1),
+                   "l2": f"{nl} disjoint block sets of the pool rotate"},
+        "per_rank": per_rank,
+        "bound": {"max_context": int(max(lens)), "sum_context": int(sum(lens)),
+                  "makespan_bound_tokens": bound_tokens,
+                  "max_rank_tokens": max(pr["context_tokens"] for pr in per_rank),
+                  "efficiency_tokens": round(sum(lens) / world / max(
+                      pr["context_tokens"] for pr in per_rank), 4),
+                  "efficiency_bytes": round(total_bytes / world / max(
+                      pr["bytes_per_step"] for pr in per_rank), 4)},
+        "hbm_gbs_per_gpu_mean": round(total_bytes / world / (t_step * 1e-6) / 1e9, 1),
+        "frac_of_measured_peak_per_gpu": round(total_bytes / world / (t_step * 1e-6) / 1e9
+                                               / peak, 4),
+        "peak_kind": peak_kind,
+        "gpu_launches": steps * world,
+    }
+
+
+# ------------------------------------------------ ragged step (config 3)
+RAGGED = ("continuous-batching step: 252 decode seqs (ctx lognormal median 1024, sigma 1, "
+          "clip [16, 8192]) + 4 prompt chunks U[256, 2048], 16q/2kv heads, hd128, bs16, fp16")
+
+
+def run_ragged(args, local):
+    """Config 3 on one GPU: per step RoPE + cache write of every packed token
+    (~4.9k), decode attention of the 252 decode sequences and causal prefill
+    attention of the 4 prompt chunks; positions and slots built on the device
+    from the block tables. Kernels timed alone and as the whole step."""
+    from cscr import attention as A
+    from cscr import pos_encoding as PE
+    from paged_decode import roofline as R
+    from paged_decode import workloads as W
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    nl = args.layers
+    layers = [W.make_batch(W.ragged_batch(args.seed + 7 * l), device=dev) for l in range(nl)]
+    H, KVH, D = 16, 2, 128
+    stream = torch.cuda.Stream(dev)
+    prep = []
+    for b in layers:
+        T = b.query.shape[0]
+        npt = b.num_prompt_tokens
+        lens = b.spec.prefill_lens
+        starts = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+        tables = torch.stack([b.token_block_tables[int(starts[c])] for c in range(len(lens))])
+        prep.append(dict(T=T, npt=npt, tables=tables.contiguous(), maxq=int(max(lens)),
+                         qs=torch.from_numpy(starts).to(dev),
+                         ctx=torch.tensor(lens, dtype=torch.int32, device=dev),
+                         out=torch.empty(T, H, D, dtype=torch.float16, device=dev)))
+
+    def rope(b, x):
+        return PE.rotary_embedding_neox_with_cache(b.positions, b.query.view(x["T"], -1),
+                                                   b.key.view(x["T"], -1), b.value,
+                                                   b.key_cache, b.value_cache, b.slot_mapping,
+                                                   D, b.cos_sin_cache)
+
+    def decode(b, x, q):
+        return A.paged_attention(q[x["npt"]:], b.key_cache, b.value_cache, b.block_tables,
+                                 b.seq_lens, b.scale)
+
+    def prefill(b, x, q):
+        return A.paged_prefill_attention(q[:x["npt"]], b.key_cache, b.value_cache, x["tables"],
+                                         x["qs"], x["ctx"], b.scale, max_query_len=x["maxq"],
+                                         out=x["out"][:x["npt"]])
+
+    qrot = [rope(b, x).view(x["T"], H, D) for b, x in zip(layers, prep)]  # warm + inputs
+    legs = {
+        "rope_cache_write": lambda i: rope(layers[i], prep[i]),
+        "decode_attention": lambda i: decode(layers[i], prep[i], qrot[i]),
+        "prefill_attention": lambda i: prefill(layers[i], prep[i], qrot[i]),
+        "step": lambda i: (lambda q: (decode(layers[i], prep[i], q),
+                                      prefill(layers[i], prep[i], q)))(
+            rope(layers[i], prep[i]).view(prep[i]["T"], H, D)),
+    }
+    times = {}
+    reps = max(1, args.steps // nl)
+    for name, fn in legs.items():
+        with torch.cuda.stream(stream):
+            for i in range(nl):
+                fn(i)
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(nl):
+                    fn(i)
+        ms, _ = _timed_graph(g, stream, dev, reps, 3, 1, lambda: None)
+        times[name] = ms * 1e3 / (reps * nl)
+        del g
+    lens_dec = [b.seq_lens.cpu().numpy() for b in layers]
+    dec_bytes = statistics.fmean(R.attention_bytes(l, 16, H, KVH, D, 2) for l in lens_dec)
+    T_mean = statistics.fmean(x["T"] for x in prep)
+    rope_b = R.rope_bytes(T_mean, H, KVH, D, D, 2) + R.cache_write_bytes(T_mean, KVH, D, 2)
+    pre_flops = statistics.fmean(
+        sum(4 * H * D * n * (n + 1) / 2 for n in b.spec.prefill_lens) for b in layers)
+    peak, peak_kind = measured_hbm_peak()
+    tflops_peak = measured_tensor_peak()
+    n_dec = len(lens_dec[0])
+    return {
+        "metric": METRIC, "value": round(n_dec / (times["step"] * 1e-6), 1), "unit": UNIT,
+        "n_gpus": 1, "steps": reps * nl, "warmup": 3 * nl, "ms_per_step": round(
+            times["step"] / 1e3, 6), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) q/k/v and KV pool, seeded lengths)",
+        "config": {"workload": RAGGED, "decode_seqs": n_dec, "packed_tokens": round(T_mean),
+                   "l2": f"{nl} rotating independent pools",
+                   "value_is": "decode tokens per second of the whole step (RoPE + cache "
+                               "write of all tokens, decode and prefill attention)"},
+        "us": {k: round(v, 3) for k, v in times.items()},
+        "roofline": {
+            "rope_cache_write": {"bound": "hbm", "bytes": int(rope_b), "achieved": round(
+                rope_b / (times["rope_cache_write"] * 1e-6) / 1e9, 1), "unit": "GB/s",
+                "frac": round(rope_b / (times["rope_cache_write"] * 1e-6) / 1e9 / peak, 4)},
+            "decode_attention": {"bound": "hbm", "bytes": int(dec_bytes), "achieved": round(
+                dec_bytes / (times["decode_attention"] * 1e-6) / 1e9, 1), "unit": "GB/s",
+                "frac": round(dec_bytes / (times["decode_attention"] * 1e-6) / 1e9 / peak, 4)},
+            "prefill_attention": {"bound": "tensor", "flops": int(pre_flops), "achieved": round(
+                pre_flops / (times["prefill_attention"] * 1e-6) / 1e12, 1), "unit": "TFLOP/s",
+                "frac": round(pre_flops / (times["prefill_attention"] * 1e-6) / 1e12
+                              / tflops_peak[0], 4), "peak": tflops_peak[0],
+                "peak_kind": tflops_peak[1]},
+            "hbm_peak": peak, "hbm_peak_kind": peak_kind},
+        "gpu_launches": 3 * reps * nl,
+    }
+
+
 # ------------------------------------------------------------ CPU side
 def oracle_inputs(batch):
     """Host copies of one layer's decode step, pool cut to the blocks it uses."""
@@ -828,6 +1094,10 @@ def main():
         sys.exit(2)
     if args.impl == "reference":
         line = run_reference(args, rank, world)
+    elif args.workload == "long_tail":
+        line = run_long_tail(args, rank, world, local)
+    elif args.workload == "ragged":
+        line = run_ragged(args, local) if rank == 0 else None
     else:
         line = run_ours(args, rank, world, local)
     if line is not None:

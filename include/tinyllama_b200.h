@@ -204,6 +204,36 @@ TLB_API int tlb_paged_attention_with_rope(void* out, const void* query, void* ke
                         size_t workspace_bytes, unsigned flags, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Prefill (multi-token, causal) paged attention over prompt chunks.
+ *
+ * No reference counterpart: the reference layer accepts decode batches only
+ * (src/model_executor/layers/attention.py:139-143). Chunk c holds the query
+ * rows query_start[c] .. query_start[c + 1] - 1 of the packed `query`; they are
+ * the last n_c = query_start[c + 1] - query_start[c] of the first
+ * context_lens[c] tokens of the chunk's sequence, whose keys and values are
+ * already in the paged cache. Row j attends to tokens 0 .. p of the sequence,
+ * p = context_lens[c] - n_c + j (causal), with the decode op's rules: query
+ * head h uses kv head h / (num_heads / num_kv_heads), negative block ids are
+ * skipped, an empty softmax gives zeros (tests/test_paged_attention.py:42-57
+ * with a causal mask is the definition).
+ *
+ *   out, query   : [num_tokens, num_heads, head_dim] (rows of all chunks)
+ *   block_tables : [num_chunks, max_blocks_per_seq] int32
+ *   query_start  : [num_chunks + 1] int32, non-decreasing
+ *   context_lens : [num_chunks] int32
+ *   max_query_len: >= every chunk's n_c (sizes the grid)
+ * fp16 / bf16, head_dim 64 or 128, 16-byte aligned tensors. Rows of `out`
+ * outside every chunk are not written.
+ * ---------------------------------------------------------------------- */
+TLB_API int tlb_paged_prefill_attention(void* out, const void* query, const void* key_cache,
+                        const void* value_cache, const int32_t* block_tables,
+                        const int32_t* query_start, const int32_t* context_lens,
+                        int64_t num_chunks, int64_t num_heads, int64_t num_kv_heads,
+                        int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                        int64_t max_blocks_per_seq, int64_t max_query_len, float scale,
+                        int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * NeoX rotary embedding.
  *
  * Replaces `rotary_embedding_neox(postions, query, key, head_size,

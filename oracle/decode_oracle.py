@@ -150,6 +150,65 @@ def paged_attention_threads(query, key_cache, value_cache, block_tables, seq_len
                                dtype, threads)
 
 
+def paged_prefill_attention_f32(query, key_cache, value_cache, block_tables, query_start,
+                                context_lens, scale, dtype, threads: int | None = None):
+    """Causal attention of prompt chunks over their paged context, fp32.
+
+    The reference has no prefill op (its layer is decode-only,
+    src/model_executor/layers/attention.py:139-143). This is the reference
+    test's math (tests/test_paged_attention.py:42-57: gather the sequence's
+    blocks, fold query heads onto their kv head, fp32 softmax(scale q K^T) V)
+    with a causal mask: row j of chunk c, at position
+    p = context_lens[c] - n_c + j, sees tokens 0..p of its sequence. Blocks
+    with a negative id are skipped; an empty softmax gives zeros.
+    Returns [T, H, D] fp32; rows outside every chunk stay zero.
+    """
+    T, H, D = query.shape
+    NB, KVH, BS, _ = key_cache.shape
+    G = H // KVH
+    q32 = to_f32(query, dtype)
+    out = np.zeros((T, H, D), np.float32)
+    qs = np.asarray(query_start, np.int64)
+
+    def chunk(c):
+        n = int(qs[c + 1] - qs[c])
+        ctx = int(context_lens[c])
+        if n <= 0:
+            return
+        first = ctx - n
+        L = max(0, min(ctx, block_tables.shape[1] * BS))
+        tok = np.arange(L)
+        blk = np.asarray(block_tables[c], np.int64)[tok // BS]
+        valid = (blk >= 0) & (blk < NB)
+        keys = np.zeros((L, KVH, D), np.float32)
+        vals = np.zeros((L, KVH, D), np.float32)
+        keys[valid] = to_f32(key_cache[blk[valid], :, (tok % BS)[valid], :], dtype)
+        vals[valid] = to_f32(value_cache[blk[valid], :, (tok % BS)[valid], :], dtype)
+        q = q32[qs[c]:qs[c] + n].reshape(n, KVH, G, D)
+        pos = first + np.arange(n)
+        allowed = valid[None, :] & (tok[None, :] <= pos[:, None])  # [n, L]
+        for h in range(KVH):
+            qh = np.ascontiguousarray(q[:, h].transpose(1, 0, 2))        # [G, n, D]
+            sc = np.matmul(qh, np.ascontiguousarray(keys[:, h].T)) * np.float32(scale)
+            sc = np.where(allowed[None], sc, np.float32(-np.inf))       # [G, n, L]
+            m = sc.max(axis=-1, keepdims=True)
+            m = np.where(np.isfinite(m), m, np.float32(0.0))
+            pr = np.exp(sc - m)
+            den = pr.sum(axis=-1, keepdims=True)
+            pr = np.divide(pr, den, out=np.zeros_like(pr), where=den > 0)
+            o = np.matmul(pr, np.ascontiguousarray(vals[:, h]))         # [G, n, D]
+            out[qs[c]:qs[c] + n, h * G:(h + 1) * G] = o.transpose(1, 0, 2)
+
+    nchunks = len(context_lens)
+    if (threads or 1) > 1 and nchunks > 1:
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(chunk, range(nchunks)))
+    else:
+        for c in range(nchunks):
+            chunk(c)
+    return out
+
+
 # ------------------------------------------------------------------ RoPE
 def rotary_embedding_neox(positions, query, key, head_size, cos_sin_cache, dtype):
     """NeoX rotary embedding; returns (out, key_rotated) in the storage dtype.
@@ -302,7 +361,8 @@ def ceil_div(a, b):
 
 __all__ = [
     "DTYPES", "bf16_bits_to_f32", "f32_to_bf16_bits", "to_f32", "from_f32", "storage_np_dtype",
-    "paged_attention", "paged_attention_f32", "paged_attention_threads", "rotary_embedding_neox", "cos_sin_cache",
+    "paged_attention", "paged_attention_f32", "paged_attention_threads",
+    "paged_prefill_attention_f32", "rotary_embedding_neox", "cos_sin_cache",
     "write_kv_cache", "reshape_and_cache", "decode_metadata", "step_metadata", "copy_blocks", "swap_blocks",
     "ceil_div",
 ]

@@ -164,3 +164,34 @@ def test_attention_oracle_semantics_edge_cases():
     bt2 = np.array([[3, 4, 0]], np.int32)
     out2 = O.paged_attention(q[1:2], kc, vc, bt2, np.array([8], np.int32), 0.25, "float32")
     np.testing.assert_allclose(out[1], out2[0], rtol=1e-6, atol=1e-6)
+
+
+def test_prefill_oracle_is_causal_and_ends_in_the_pinned_decode_oracle():
+    """The prefill oracle (no reference op exists) against the pinned decode
+    oracle: the last row of every chunk is decode attention over the whole
+    context, the first row of a fresh prompt sees token 0 only, and changing
+    a later token leaves every earlier row unchanged."""
+    rng = np.random.default_rng(1)
+    H, KVH, D, BS = 8, 2, 64, 8
+    lens, ctx = [12, 1, 30], [12, 50, 30]
+    T = sum(lens)
+    q = rng.standard_normal((T, H, D)).astype(np.float32)
+    kc = rng.standard_normal((40, KVH, BS, D)).astype(np.float32)
+    vc = rng.standard_normal((40, KVH, BS, D)).astype(np.float32)
+    bt = np.full((3, 8), -1, np.int32)
+    bt[0, :2] = [3, 9]
+    bt[1, :7] = [1, 2, 4, 5, 6, 7, 8]
+    bt[2, :4] = [10, 11, 12, 13]
+    qs = np.array([0, 12, 13, 43])
+    out = O.paged_prefill_attention_f32(q, kc, vc, bt, qs, ctx, 0.125, "float32")
+    last = qs[1:] - 1
+    dec = O.paged_attention_f32(q[last], kc, vc, bt, np.asarray(ctx), 0.125, "float32")
+    np.testing.assert_allclose(out[last], dec, atol=1e-5, rtol=1e-5)
+    group = H // KVH
+    for h in range(H):
+        np.testing.assert_allclose(out[0, h], vc[3, h // group, 0], atol=1e-6)
+    kc2 = kc.copy()
+    kc2[11, :, 3] += 5.0  # token 8 + 3 = 11 of chunk 2
+    out2 = O.paged_prefill_attention_f32(q, kc2, vc, bt, qs, ctx, 0.125, "float32")
+    np.testing.assert_array_equal(out2[13:13 + 11], out[13:13 + 11])
+    assert not np.allclose(out2[13 + 11:43], out[13 + 11:43])

@@ -48,6 +48,8 @@ _PROTOS = {
     "tlb_paged_attention_with_rope": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32,
                                       _vp, _sz, ctypes.c_uint, _vp],
+    "tlb_paged_prefill_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                    _i64, _i64, _i64, _i64, _f32, _i32, _vp],
     "tlb_rotary_embedding_neox": [_vp, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64,
                                   _i64, _i64, _i64, _i64, _i32, _vp],
     "tlb_reshape_and_cache": [_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -228,3 +228,58 @@ def paged_attention_with_rope(query: torch.Tensor, key: torch.Tensor, value: tor
         cos_sin_cache, block_tables=block_tables)
     return paged_attention(q_rot.view(num_seqs, num_heads, head_dim), key_cache, value_cache,
                            block_tables, seq_lens, scale)
+
+
+def paged_prefill_attention(query: torch.Tensor, key_cache: torch.Tensor,
+                            value_cache: torch.Tensor, block_tables: torch.Tensor,
+                            query_start: torch.Tensor, context_lens: torch.Tensor, scale: float,
+                            max_query_len: int | None = None,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal paged attention of prompt chunks (not in the reference API, whose
+    layer is decode-only: src/model_executor/layers/attention.py:139-143).
+
+    query [num_tokens, num_heads, head_dim]: chunk c owns rows
+    query_start[c] .. query_start[c + 1] - 1, the last tokens of the first
+    context_lens[c] tokens of its sequence, whose keys and values are already
+    in the caches (run the RoPE + cache write over the packed step first).
+    block_tables [num_chunks, max_blocks] int32, query_start [num_chunks + 1]
+    int32, context_lens [num_chunks] int32. ``max_query_len`` (the longest
+    chunk) sizes the launch; when omitted it is read from query_start (a
+    device-to-host read). Returns ``out`` (a new tensor unless given); rows
+    outside every chunk are left as they were.
+    """
+    torch_check(query.is_cuda and key_cache.is_cuda and value_cache.is_cuda
+                and block_tables.is_cuda and query_start.is_cuda and context_lens.is_cuda,
+                "all tensors must be CUDA tensors")
+    torch_check(query.dim() == 3 and query.is_contiguous(),
+                "query must be a contiguous [num_tokens, num_heads, head_dim] tensor")
+    torch_check(key_cache.dim() == 4 and key_cache.shape == value_cache.shape
+                and key_cache.is_contiguous() and value_cache.is_contiguous(),
+                "key_cache and value_cache must be contiguous [num_blocks, num_kv_heads, "
+                "block_size, head_dim] tensors of one shape")
+    torch_check(query.dtype in (torch.float16, torch.bfloat16)
+                and key_cache.dtype == query.dtype and value_cache.dtype == query.dtype,
+                "prefill attention supports float16 and bfloat16 (query and caches alike)")
+    torch_check(block_tables.dtype == torch.int32 and query_start.dtype == torch.int32
+                and context_lens.dtype == torch.int32,
+                "block_tables, query_start and context_lens must be int32")
+    num_chunks = context_lens.numel()
+    torch_check(block_tables.dim() == 2 and block_tables.size(0) == num_chunks
+                and query_start.numel() == num_chunks + 1,
+                "one block-table row and one context length per chunk, num_chunks + 1 starts")
+    T, H, D = query.shape
+    torch_check(key_cache.size(3) == D, "query head_dim must match the cache head_dim")
+    if out is None:
+        out = torch.empty_like(query)
+    if max_query_len is None:
+        max_query_len = int((query_start[1:] - query_start[:-1]).max().item()) if num_chunks else 0
+    dev = query.device
+    with _lib.device_guard(dev):
+        rc = _lib.load().tlb_paged_prefill_attention(
+            out.data_ptr(), query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            block_tables.contiguous().data_ptr(), query_start.contiguous().data_ptr(),
+            context_lens.contiguous().data_ptr(), num_chunks, H, key_cache.size(1), D,
+            key_cache.size(0), key_cache.size(2), block_tables.size(1), int(max_query_len),
+            float(scale), DTYPE_CODE[query.dtype], _lib.stream_of(dev))
+        _lib.check(rc)
+    return out

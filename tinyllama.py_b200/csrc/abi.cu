@@ -194,6 +194,41 @@ int tlb_get_device_status(uint32_t* status_out, int clear, void* stream) {
     return TLB_OK;
 }
 
+// ------------------------------------------------------------ prefill
+int tlb_paged_prefill_attention(void* out, const void* query, const void* key_cache,
+                                const void* value_cache, const int32_t* block_tables,
+                                const int32_t* query_start, const int32_t* context_lens,
+                                int64_t num_chunks, int64_t num_heads, int64_t num_kv_heads,
+                                int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                int64_t max_blocks_per_seq, int64_t max_query_len, float scale,
+                                int dtype, void* stream) {
+    TLB_REQUIRE(dtype == TLB_FLOAT16 || dtype == TLB_BFLOAT16,
+                "prefill attention supports float16 and bfloat16");
+    TLB_REQUIRE(head_dim == 64 || head_dim == 128, "prefill attention supports head_dim 64 or 128");
+    TLB_REQUIRE(num_chunks >= 0 && max_query_len >= 0, "counts must not be negative");
+    TLB_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_blocks > 0 && block_size > 0 &&
+                    max_blocks_per_seq > 0,
+                "sizes must be positive");
+    TLB_REQUIRE(num_heads % num_kv_heads == 0, "num_heads must be divisible by num_kv_heads");
+    TLB_REQUIRE(num_chunks < 65536 && num_heads < 65536 && max_query_len < (1ll << 22) &&
+                    max_blocks_per_seq * block_size < (1ll << 31),
+                "sizes exceed the supported range");
+    if (num_chunks == 0 || max_query_len == 0) return TLB_OK;
+    TLB_REQUIRE(out && query && key_cache && value_cache && block_tables && query_start &&
+                    context_lens,
+                "tensor pointers must not be null");
+    TLB_REQUIRE(aligned(out, 16) && aligned(query, 16) && aligned(key_cache, 16) &&
+                    aligned(value_cache, 16),
+                "query, out and the caches must be 16-byte aligned");
+    cudaError_t e = tlb::launch_prefill_attention(
+        dtype, (int)head_dim, out, query, key_cache, value_cache, block_tables, query_start,
+        context_lens, num_blocks, (int)num_chunks, (int)num_heads, (int)num_kv_heads,
+        (int)block_size, (int)max_blocks_per_seq, (int)max_query_len,
+        scale * 1.4426950408889634f, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "launching prefill attention");
+    return TLB_OK;
+}
+
 // ------------------------------------------------------------ attention
 int tlb_paged_attention_workspace_size(int64_t num_seqs, int64_t num_heads, int64_t num_kv_heads,
                                        int64_t head_dim, int dtype, size_t* bytes_out) {

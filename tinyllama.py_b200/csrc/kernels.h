@@ -166,6 +166,15 @@ cudaError_t launch_step_metadata(const int32_t* prompt_lens, const int32_t* prom
                                  long long num_padded, int64_t* positions, int64_t* slots,
                                  cudaStream_t stream);
 
+// Causal paged attention of prompt chunks (prefill_attention.cu).
+cudaError_t launch_prefill_attention(int dtype, int head_dim, void* out, const void* query,
+                                     const void* key_cache, const void* value_cache,
+                                     const int32_t* block_tables, const int32_t* query_start,
+                                     const int32_t* context_lens, long long num_blocks,
+                                     int num_chunks, int num_heads, int num_kv_heads,
+                                     int block_size, int max_blocks, int max_query_len,
+                                     float scale_log2, cudaStream_t stream);
+
 // ------------------------------------------------------------ block copies
 constexpr int kCopyMaxCaches = 128;
 constexpr int kCopyMaxPairs = 1024;

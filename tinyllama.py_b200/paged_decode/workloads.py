@@ -161,8 +161,14 @@ class DecodeBatch:
 
 
 def make_batch(spec: DecodeSpec, device="cuda", fill_cache: bool = True,
-               build_dtype: torch.dtype | None = None) -> DecodeBatch:
-    """Materialise a decode step for `spec` on `device`."""
+               build_dtype: torch.dtype | None = None,
+               caches: tuple[torch.Tensor, torch.Tensor] | None = None) -> DecodeBatch:
+    """Materialise a decode step for `spec` on `device`.
+
+    ``caches``: an existing (key_cache, value_cache) pool of ``spec.num_blocks``
+    blocks to place the batch in (a large per-GPU pool shared by several
+    steps); only the blocks the batch uses are filled, with N(0, 1) values.
+    """
     dev = torch.device(device)
     dtype = TORCH_DTYPES[spec.dtype]
     bs, H, KVH, D = spec.block_size, spec.num_heads, spec.num_kv_heads, spec.head_dim
@@ -220,7 +226,18 @@ def make_batch(spec: DecodeSpec, device="cuda", fill_cache: bool = True,
     query = randn(T, H, D, generator=g)
     key = randn(T, KVH, D, generator=g)
     value = randn(T, KVH, D, generator=g)
-    if fill_cache:
+    if caches is not None:
+        kc, vc = caches
+        if tuple(kc.shape) != (NB, KVH, bs, D) or kc.shape != vc.shape or kc.dtype != dtype:
+            raise ValueError("caches must be two [num_blocks, kv_heads, block_size, head_dim] "
+                             "tensors of the batch dtype")
+        if fill_cache and need:
+            idx = torch.from_numpy(perm).to(kc.device)
+            for c in (kc, vc):
+                c.index_copy_(0, idx, torch.randn(need, KVH, bs, D, generator=gen_dev,
+                                                  device=gen_dev.device,
+                                                  dtype=torch.float32).to(dtype).to(dev))
+    elif fill_cache:
         kc = torch.randn(NB, KVH, bs, D, generator=gen_dev, device=gen_dev.device,
                          dtype=dtype if dev.type == "cuda" else torch.float32).to(dtype).to(dev)
         vc = torch.randn(NB, KVH, bs, D, generator=gen_dev, device=gen_dev.device,
