@@ -239,3 +239,41 @@ def test_reference_modules_do_not_shadow_the_product_package():
     assert sys.modules["cscr.attention"] is mine
     assert mine.paged_attention is A.paged_attention
     assert mine.__file__.endswith("tinyllama.py_b200/cscr/attention.py")
+
+
+def test_copy_blocks_speed_beside_the_reference_kernel(ref_cache, record_property):
+    """Copy-on-write fan-out over a 36-layer cache (72 caches, 256 block pairs
+    each, 151 MB copied, more than the L2): this repository's one-launch copy
+    and the reference's copy_blocks (cache_kernel.cu:180-212: a synchronous
+    mapping upload, then one launch per cache), timed with CUDA events.
+    Reported, with identical results asserted; the rate is not asserted."""
+    NB, KVH, bs, D, L = 4096, 2, 16, 128, 36
+    g = torch.Generator(device="cuda").manual_seed(11)
+    caches = [torch.randn(NB, KVH, bs, D, generator=g, device="cuda").to(torch.bfloat16)
+              for _ in range(2 * L)]
+    mine = [c.clone() for c in caches]
+    perm = torch.randperm(NB, generator=torch.Generator().manual_seed(3)).tolist()
+    mapping = {perm[i]: [perm[256 + i]] for i in range(256)}
+    block_bytes = KVH * bs * D * 2
+    moved = 2 * 256 * 2 * L * block_bytes  # read + write of every copied block
+
+    def timed(fn, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    t_ref = timed(lambda: ref_cache.copy_blocks(key_caches=caches[:L], value_caches=caches[L:],
+                                                block_mapping=mapping))
+    t_ours = timed(lambda: C.copy_blocks(mine[:L], mine[L:], mapping))
+    for a, b in zip(caches, mine):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    record_property("us_reference", round(t_ref, 2))
+    record_property("us_ours", round(t_ours, 2))
+    print(f"[copy_blocks 36 layers, 256 pairs] reference {t_ref:.1f} us "
+          f"({moved / t_ref / 1e3:.0f} GB/s), ours {t_ours:.1f} us ({moved / t_ours / 1e3:.0f} GB/s)")

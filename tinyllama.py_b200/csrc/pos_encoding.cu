@@ -123,8 +123,11 @@ __device__ __forceinline__ void rotate(const T* src, T* dst, const T* cs, int ha
 //   [.., + nk_rot)         key rotation (in place; to the cache when WITH_CACHE)
 //   [.., + nk_pass)        WITH_CACHE: key elements >= rot copied to the cache
 //   [.., + nv)             WITH_CACHE: value row copied to the cache
+// IX is the index type of the item arithmetic: 32-bit unsigned when the
+// launch has fewer than 2^31 items (the usual case; its divisions are a few
+// instructions), 64-bit otherwise.
 template <typename T, typename PI, typename SI, int VEC, bool WITH_QUERY, bool WITH_CACHE,
-          bool BY_TABLE>
+          bool BY_TABLE, typename IX>
 __global__ void __launch_bounds__(256) rope_cache_kernel(const RopeCacheParams p) {
     // A kernel launched after this one with programmatic serialization (the
     // attention kernel) may start its metadata prologue now; it still waits
@@ -137,17 +140,17 @@ __global__ void __launch_bounds__(256) rope_cache_kernel(const RopeCacheParams p
     // the kernel before it (the QKV projection in a model) produces - and it
     // writes nothing. Without a programmatic launch the wait returns at once.
     const int half = p.rot_dim / 2;
-    const int hv = half / VEC;                       // pair vectors per head
-    const int pv = (p.head_size - p.rot_dim) / VEC;  // pass-through vectors per head
-    const int dv = p.head_size / VEC;
-    const long long nq_rot = WITH_QUERY ? (long long)p.num_heads * hv : 0;
-    const long long nq_pass = WITH_QUERY ? (long long)p.num_heads * pv : 0;
-    const long long nk_rot = WITH_QUERY ? (long long)p.num_kv_heads * hv : 0;
-    const long long nk_pass = WITH_CACHE && WITH_QUERY ? (long long)p.num_kv_heads * pv : 0;
-    const long long nk_copy = WITH_CACHE && !WITH_QUERY ? (long long)p.num_kv_heads * dv : 0;
-    const long long nv = WITH_CACHE ? (long long)p.num_kv_heads * dv : 0;
-    const long long per_tok = nq_rot + nq_pass + nk_rot + nk_pass + nk_copy + nv;
-    const long long total = per_tok * p.num_tokens;
+    const IX hv = (IX)(half / VEC);                       // pair vectors per head
+    const IX pv = (IX)((p.head_size - p.rot_dim) / VEC);  // pass-through vectors per head
+    const IX dv = (IX)(p.head_size / VEC);
+    const IX nq_rot = WITH_QUERY ? (IX)p.num_heads * hv : 0;
+    const IX nq_pass = WITH_QUERY ? (IX)p.num_heads * pv : 0;
+    const IX nk_rot = WITH_QUERY ? (IX)p.num_kv_heads * hv : 0;
+    const IX nk_pass = WITH_CACHE && WITH_QUERY ? (IX)p.num_kv_heads * pv : 0;
+    const IX nk_copy = WITH_CACHE && !WITH_QUERY ? (IX)p.num_kv_heads * dv : 0;
+    const IX nv = WITH_CACHE ? (IX)p.num_kv_heads * dv : 0;
+    const IX per_tok = nq_rot + nq_pass + nk_rot + nk_pass + nk_copy + nv;
+    const IX total = per_tok * (IX)p.num_tokens;
 
     const T* query = reinterpret_cast<const T*>(p.query);
     T* key = reinterpret_cast<T*>(p.key);
@@ -157,10 +160,10 @@ __global__ void __launch_bounds__(256) rope_cache_kernel(const RopeCacheParams p
     T* vc = reinterpret_cast<T*>(p.value_cache);
     const T* cs_all = reinterpret_cast<const T*>(p.cos_sin);
 
-    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (long long)gridDim.x * blockDim.x) {
-        const long long t = idx / per_tok;
-        long long r = idx - t * per_tok;
+    for (IX idx = (IX)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (IX)gridDim.x * blockDim.x) {
+        const long long t = (long long)(idx / per_tok);
+        IX r = idx - (IX)t * per_tok;
 
         long long pos = 0;
         const T* cs = nullptr;
@@ -294,7 +297,10 @@ cudaError_t go(const RopeCacheParams& p, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = p.overlap ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, rope_cache_kernel<T, PI, SI, VEC, Q, C, BT>, p);
+    if (items < (1ll << 31))
+        return cudaLaunchKernelEx(&cfg, rope_cache_kernel<T, PI, SI, VEC, Q, C, BT, unsigned>, p);
+    return cudaLaunchKernelEx(&cfg, rope_cache_kernel<T, PI, SI, VEC, Q, C, BT,
+                                                      unsigned long long>, p);
 }
 
 template <typename T, int VEC, bool Q, bool C, bool BT>

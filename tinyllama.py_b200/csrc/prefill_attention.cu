@@ -13,51 +13,36 @@
 // negative id are skipped and a softmax with nothing left gives zeros, the
 // decode op's rules (cscr/attention_kernel.cu:70-72, :102).
 //
-// One CTA takes 64 query tokens of one query head (four warps x 16 rows) and
-// walks the 64-token KV tiles up to its last query's position:
-//   * K and V tiles come from the paged cache with 16-byte cp.async copies
-//     into a two-buffer ring (the next tile loads while this one computes),
-//     rows XOR-swizzled by 16-byte chunk so that ldmatrix is conflict-free;
-//     rows past the causal limit or in unmapped blocks are zero-filled and
-//     masked.
-//   * S = Q K^T and O += P V with mma.m16n8k16 (fp32 accumulate), the query
-//     fragments held in registers for the whole walk, an fp32 online softmax
-//     in registers (quad shuffles), P fed from the S accumulators (for bf16
-//     as a hi + lo pair, 16 significant bits, like the decode kernel).
-//   * CTAs of the late (heavier) query tiles are scheduled first.
-// Query heads of one kv head run as neighbouring CTAs, so a KV tile is read
-// from HBM about once and from L2 by the rest of the group.
+// The contractions run on the 5th-generation tensor cores (tcgen05) with
+// their accumulators in tensor memory. One CTA takes 128 query rows of one
+// query head (tensor-memory lane r = query row r, owned by thread r for the
+// softmax) and walks 64-token KV tiles up to its last query's position:
+//   * Q (once), K and V come from the paged cache with 16-byte cp.async
+//     copies into 128-byte-swizzled shared memory; rows past the causal
+//     limit or in unmapped blocks are zero-filled and marked unusable. K is
+//     single-buffered, V double-buffered: the next tile's copies start as
+//     soon as the current S = Q K^T has completed (which also means the
+//     previous tile's P V has, so its V buffer and P are free).
+//   * S = Q K^T: M 128 x N 64, K = head dim, Q and K K-major, S in tensor
+//     memory. Each thread loads its row of S (tcgen05.ld), masks, updates the
+//     fp32 online softmax (base 2) and, when its running maximum moved,
+//     rescales its row of O in tensor memory (tcgen05.ld / st).
+//   * P (the row's probabilities in the storage type) goes to shared memory
+//     K-major; O += P V: M 128 x N = head dim, K 64 tokens, V read MN-major
+//     straight from its copied tile. One thread issues every MMA; commits to
+//     mbarriers order them against the threads.
+//   * CTAs of the late (heavier) query tiles are scheduled first. Query heads
+//     of one kv head are neighbouring CTAs, so a KV tile comes from HBM about
+//     once and from L2 for the rest of the group.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace tlb {
 namespace prefill {
 namespace {
-
-constexpr int kBQ = 64;       // query tokens per CTA (4 warps x 16 rows)
-constexpr int kBK = 64;       // KV tokens per tile
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-
-template <int D>
-struct Layout {
-    static constexpr int kRowBytes = D * 2;
-    static constexpr int kChunks = D / 8;               // 16-byte chunks per row
-    static constexpr int kTile = kBK * kRowBytes;       // one K or V tile
-    static constexpr int kOffQ = 0;
-    static constexpr int kOffK = kOffQ + kBQ * kRowBytes;
-    static constexpr int kOffV = kOffK + 2 * kTile;
-    static constexpr int kOffOk = kOffV + 2 * kTile;   // [2][kBK] row usable
-    static constexpr int kBytes = kOffOk + 2 * kBK;
-};
-
-// Byte offset of 16-byte chunk `ch` of row `row` in a swizzled tile: the
-// chunk index is XORed with the row's low three bits, so the eight rows an
-// ldmatrix reads at one logical chunk fall in eight different bank groups.
-template <int D>
-__device__ __forceinline__ uint32_t swz(int row, int ch) {
-    return (uint32_t)(row * (D * 2) + ((ch ^ (row & 7)) << 4));
-}
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool pred) {
     // src-size 0 fills the 16 bytes with zeros and reads nothing
@@ -85,22 +70,60 @@ struct Params {
     float scale_log2;
 };
 
-// Loads KV tile `kt` (tokens kt*64 .. +63) of kv head `kvh` into buffer
-// `buf`: one 16-byte cp.async per (row, chunk); rows at or past `kv_end`, and
-// rows whose block id is negative or outside the pool, are zero-filled and
-// marked unusable in `ok`.
-template <typename T, int D>
-__device__ __forceinline__ void load_kv_tile(const Params& p, uint8_t* smem, uint32_t sbase,
-                                             int buf, int kt, int c, int kvh, int kv_end) {
-    using L = Layout<D>;
+// ---------------------------------------------------------------- tcgen05
+// One CTA = 128 query rows of one query head (tensor-memory lane r = row r,
+// thread r its softmax), KV tiles of 64 tokens.
+constexpr int kTcBQ = 128;
+constexpr int kTcBK = 64;
+constexpr int kTcThreads = 128;
+
+// With bf16 the probabilities go to the PV product as a hi + lo pair of bf16
+// values (16 significant bits, as in the decode kernel; bf16 alone keeps 8):
+// the layout then holds two P tiles and one V buffer instead of one P tile
+// and two V buffers (the same bytes, so two CTAs still fit an SM).
+template <int D, bool SPLIT>
+struct TcLayout {
+    static constexpr int kCh = D / 64;                       // 64-element chunks of a row
+    static constexpr int kVBufs = SPLIT ? 1 : 2;
+    static constexpr int kPTiles = SPLIT ? 2 : 1;
+    static constexpr int kOffQ = 0;                          // [kCh][128 rows][128 B]
+    static constexpr int kOffK = kOffQ + kCh * kTcBQ * 128;  // [kCh][64 tokens][128 B]
+    static constexpr int kOffV = kOffK + kCh * kTcBK * 128;  // kVBufs buffers of the same
+    static constexpr int kVBuf = kCh * kTcBK * 128;
+    static constexpr int kOffP = kOffV + kVBufs * kVBuf;     // [kPTiles][128 rows][128 B]
+    static constexpr int kPTile = kTcBQ * 128;               // 64 tokens of every row
+    static constexpr int kOffOk = kOffP + kPTiles * kPTile;  // [2][64] token usable
+    static constexpr int kOffBar = kOffOk + 2 * kTcBK;       // S done, O done
+    static constexpr int kOffSlot = kOffBar + 16;            // tensor-memory address
+    static constexpr int kBytes = kOffSlot + 16;
+    static constexpr int kAlloc = kBytes + 1024;             // slack for 1024-byte alignment
+    static constexpr uint32_t kTmemCols = D == 128 ? 256 : 128;  // S: 64 columns, O: D
+    static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kVBuf % 1024 == 0 &&
+                      kOffP % 1024 == 0 && kPTile % 1024 == 0,
+                  "swizzled tiles on 1024-byte boundaries");
+};
+
+// 16-byte unit `u` (of 8 per 128-byte row) of row `row` in a [rows][128 B]
+// block with 128-byte swizzle.
+__device__ __forceinline__ uint32_t sw128(int row, int u) {
+    return (uint32_t)(row * 128 + ((u ^ (row & 7)) << 4));
+}
+
+// KV tile `kt` (tokens kt*64 .. +63): K into the K buffer (and the usable
+// flag of every token into ok[kt % 2]), V into V buffer `vbuf`. Rows at or past
+// kv_end, or in a block whose id is negative or outside the pool, are
+// zero-filled and unusable.
+template <typename T, int D, bool SPLIT, bool DO_K, bool DO_V>
+__device__ __forceinline__ void load_kv_tc(const Params& p, uint8_t* smem, uint32_t sbase,
+                                           int vbuf, int kt, int c, int kvh, int kv_end) {
+    using L = TcLayout<D, SPLIT>;
     const T* kc = reinterpret_cast<const T*>(p.key_cache);
     const T* vc = reinterpret_cast<const T*>(p.value_cache);
     const int* table = p.block_tables + (long long)c * p.max_blocks;
-    const uint32_t kdst = sbase + L::kOffK + buf * L::kTile;
-    const uint32_t vdst = sbase + L::kOffV + buf * L::kTile;
-    for (int i = threadIdx.x; i < kBK * L::kChunks; i += kThreads) {
-        const int row = i / L::kChunks, ch = i % L::kChunks;
-        const int tok = kt * kBK + row;
+    constexpr int kUnits = D / 8;  // 16-byte units per row
+    for (int i = threadIdx.x; i < kTcBK * kUnits; i += kTcThreads) {
+        const int row = i / kUnits, ua = i % kUnits;
+        const int tok = kt * kTcBK + row;
         bool use = tok < kv_end;
         long long off = 0;
         if (use) {
@@ -109,195 +132,228 @@ __device__ __forceinline__ void load_kv_tile(const Params& p, uint8_t* smem, uin
                 use = false;
             } else if (blk >= p.num_blocks) {
                 use = false;
-                if (ch == 0) flag_status(TLB_STATUS_BAD_BLOCK_ID);
+                if (ua == 0) flag_status(TLB_STATUS_BAD_BLOCK_ID);
             } else {
                 off = (((long long)blk * p.num_kv_heads + kvh) * p.block_size +
-                       tok % p.block_size) * D + ch * 8;
+                       tok % p.block_size) * D + ua * 8;
             }
         }
-        cp_async_16(kdst + swz<D>(row, ch), kc + off, use);
-        cp_async_16(vdst + swz<D>(row, ch), vc + off, use);
-        if (ch == 0) smem[L::kOffOk + buf * kBK + row] = use ? 1 : 0;
+        const uint32_t dst = (uint32_t)((ua >> 3) * kTcBK * 128) + sw128(row, ua & 7);
+        if (DO_K) {
+            cp_async_16(sbase + L::kOffK + dst, kc + off, use);
+            if (ua == 0) smem[L::kOffOk + (kt & 1) * kTcBK + row] = use ? 1 : 0;
+        }
+        if (DO_V) cp_async_16(sbase + L::kOffV + vbuf * L::kVBuf + dst, vc + off, use);
     }
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 2) prefill_attention_kernel(const Params p) {
-    using L = Layout<D>;
-    constexpr int KS = D / 16;   // k-steps of Q K^T over the head dim
-    constexpr int NO = D / 8;    // n-tiles of the output (8 dims each)
-    extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __half>::value) ? 2 : 3)
+    prefill_attention_tc_kernel(const Params p) {
+    constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+    constexpr bool kSplit = kBf16;  // P as a hi + lo pair of bf16
+    using L = TcLayout<D, kSplit>;
+    constexpr uint32_t kIdescS = tc5::idesc_f16(kBf16, false, kTcBQ, kTcBK);
+    constexpr uint32_t kIdescO = tc5::idesc_f16(kBf16, true, kTcBQ, D);
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     const uint32_t sbase = smem_u32(smem);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, q4 = lane & 3;
+    const uint32_t bar_s = sbase + L::kOffBar, bar_o = bar_s + 8;
+    const int tid = threadIdx.x, warp = tid >> 5;
 
     const int c = blockIdx.z;
     const int h = blockIdx.y;
     const int tile = p.q_tiles - 1 - (int)blockIdx.x;  // late, heavier tiles first
     const int q_begin = p.query_start[c];
     const int n_c = p.query_start[c + 1] - q_begin;
-    if (tile * kBQ >= n_c) return;  // (also a chunk with no, or negative, length)
+    if (tile * kTcBQ >= n_c) return;  // (also a chunk with no, or negative, length)
     const int ctx = p.context_lens[c];
-    const int first_pos = ctx - n_c;  // position of the chunk's first query token
+    const int first_pos = ctx - n_c;
     const int kvh = h / p.group;
-    const int rows_here = min(kBQ, n_c - tile * kBQ);
-    const int cap = p.max_blocks * p.block_size;  // tokens the block table can address
-    if (ctx > cap && tile == p.q_tiles - 1 && h == 0 && threadIdx.x == 0)
+    const int rows_here = min(kTcBQ, n_c - tile * kTcBQ);
+    const int cap = p.max_blocks * p.block_size;
+    if (ctx > cap && tile == p.q_tiles - 1 && h == 0 && tid == 0)
         flag_status(TLB_STATUS_SEQ_TOO_LONG);
-    // KV tokens this tile needs: up to its last query's position
-    const int kv_end = max(0, min(min(ctx, cap), first_pos + tile * kBQ + rows_here));
-    const int n_kv_tiles = (kv_end + kBK - 1) / kBK;
+    const int kv_end = max(0, min(min(ctx, cap), first_pos + tile * kTcBQ + rows_here));
+    const int nkt = (kv_end + kTcBK - 1) / kTcBK;
 
+    // ---- query tile, first KV tile
     const T* query = reinterpret_cast<const T*>(p.query);
-    const long long tok0 = (long long)q_begin + tile * kBQ;  // packed row of query 0
-    // ---- query tile -> shared memory (zero rows past the chunk)
-    for (int i = tid; i < kBQ * L::kChunks; i += kThreads) {
-        const int row = i / L::kChunks, ch = i % L::kChunks;
+    const long long tok0 = (long long)q_begin + tile * kTcBQ;
+    constexpr int kUnits = D / 8;
+    for (int i = tid; i < kTcBQ * kUnits; i += kTcThreads) {
+        const int row = i / kUnits, ua = i % kUnits;
         const bool use = row < rows_here;
-        const T* src = query + ((tok0 + (use ? row : 0)) * p.num_heads + h) * D + ch * 8;
-        cp_async_16(sbase + L::kOffQ + swz<D>(row, ch), src, use);
+        const T* src = query + ((tok0 + (use ? row : 0)) * p.num_heads + h) * D + ua * 8;
+        cp_async_16(sbase + L::kOffQ + (uint32_t)((ua >> 3) * kTcBQ * 128) + sw128(row, ua & 7),
+                    src, use);
     }
+    if (nkt > 0) load_kv_tc<T, D, kSplit, true, true>(p, smem, sbase, 0, 0, c, kvh, kv_end);
     cp_async_commit();
-    if (n_kv_tiles > 0) load_kv_tile<T, D>(p, smem, sbase, 0, 0, c, kvh, kv_end);
-    cp_async_commit();
-
-    // this thread's two query rows (g, g + 8 of the warp's 16) and positions
-    const int r0 = warp * 16 + g;
-    const int pos0 = first_pos + tile * kBQ + r0, pos1 = pos0 + 8;
-
-    cp_async_wait<1>();
-    __syncthreads();
-    uint32_t qa[KS][4];
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-        const int row = warp * 16 + (lane & 15);
-        const int ch = ks * 2 + (lane >> 4);
-        ldsm_x4(sbase + L::kOffQ + swz<D>(row, ch), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    if (tid == 0) {
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        fence_mbar_init();
     }
-
-    float o[NO][4];
-#pragma unroll
-    for (int n = 0; n < NO; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    const float sl2 = p.scale_log2;
-
-    for (int kt = 0; kt < n_kv_tiles; ++kt) {
-        const int buf = kt & 1;
-        // the next tile loads into the other buffer while this one computes
-        // (everyone finished reading that buffer before the last barrier)
-        if (kt + 1 < n_kv_tiles) load_kv_tile<T, D>(p, smem, sbase, buf ^ 1, kt + 1, c, kvh, kv_end);
-        cp_async_commit();
-        cp_async_wait<1>();
-        __syncthreads();
-
-        const uint32_t kb = sbase + L::kOffK + buf * L::kTile;
-        const uint32_t vb = sbase + L::kOffV + buf * L::kTile;
-        const uint8_t* ok = smem + L::kOffOk + buf * kBK;
-        // ---- S = Q K^T: 16 query rows x 64 kv tokens per warp (8 n-tiles)
-        float sacc[8][4];
-#pragma unroll
-        for (int n = 0; n < 8; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
-#pragma unroll
-        for (int np = 0; np < 4; ++np) {  // pairs of n-tiles: tokens 16 np .. 16 np + 15
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                uint32_t b0, b1, b2, b3;
-                const int row = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-                const int ch = ks * 2 + ((lane >> 3) & 1);
-                ldsm_x4(kb + swz<D>(row, ch), b0, b1, b2, b3);
-                mma16816<T>(sacc[2 * np], qa[ks], b0, b1);
-                mma16816<T>(sacc[2 * np + 1], qa[ks], b2, b3);
-            }
-        }
-        // ---- causal / unmapped-block mask, online softmax (base 2)
-        float mx[2] = {m_run[0], m_run[1]};
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int col = n * 8 + 2 * q4 + (e & 1);
-                const int tok = kt * kBK + col;
-                const int qpos = (e < 2) ? pos0 : pos1;
-                const bool keep = ok[col] && tok <= qpos;
-                const float v = keep ? sacc[n][e] * sl2 : -INFINITY;
-                sacc[n][e] = v;
-                mx[e >> 1] = fmaxf(mx[e >> 1], v);
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-        }
-        float alpha[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            alpha[r] = mx[r] == -INFINITY ? 1.f : exp2f(m_run[r] - mx[r]);
-            m_run[r] = mx[r];
-        }
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float mr = m_run[e >> 1];
-                const float pv = mr == -INFINITY ? 0.f : exp2f(sacc[n][e] - mr);
-                sacc[n][e] = pv;
-                rs[e >> 1] += pv;
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-            l_run[r] = l_run[r] * alpha[r] + rs[r];
-        }
-#pragma unroll
-        for (int n = 0; n < NO; ++n) {
-            o[n][0] *= alpha[0];
-            o[n][1] *= alpha[0];
-            o[n][2] *= alpha[1];
-            o[n][3] *= alpha[1];
-        }
-        // ---- O += P V: P (16 x 64) from the S accumulators, 4 k-steps of 16
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t ph[4], pl[4];
-            split2<T>(sacc[2 * kk][0], sacc[2 * kk][1], ph[0], pl[0]);
-            split2<T>(sacc[2 * kk][2], sacc[2 * kk][3], ph[1], pl[1]);
-            split2<T>(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1], ph[2], pl[2]);
-            split2<T>(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3], ph[3], pl[3]);
-#pragma unroll
-            for (int dp = 0; dp < NO / 2; ++dp) {  // pairs of output n-tiles (16 dims)
-                uint32_t b0, b1, b2, b3;
-                const int row = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-                const int ch = dp * 2 + (lane >> 4);
-                ldsm_x4_trans(vb + swz<D>(row, ch), b0, b1, b2, b3);
-                mma16816<T>(o[2 * dp], ph, b0, b1);
-                mma16816<T>(o[2 * dp + 1], ph, b2, b3);
-                if constexpr (kSplitP<T>) {
-                    mma16816<T>(o[2 * dp], pl, b0, b1);
-                    mma16816<T>(o[2 * dp + 1], pl, b2, b3);
-                }
-            }
-        }
-        __syncthreads();  // every warp is done with `buf` before it is refilled
-    }
+    if (warp == 0) tc5::alloc(sbase + L::kOffSlot, L::kTmemCols);
     cp_async_wait<0>();
+    fence_proxy_async_smem();
+    tc5::fence_before_sync();
+    __syncthreads();
+    tc5::fence_after_sync();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::kOffSlot);
+    const uint32_t t_s = tmem, t_o = tmem + kTcBK;          // columns of S and O
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;  // this warp's lanes
+
+    const int row = tid;  // query row of this thread
+    const int qpos = first_pos + tile * kTcBQ + row;
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+
+    for (int kt = 0; kt < nkt; ++kt) {
+        const int buf = kt & 1;
+        // ---- S = Q K^T (M 128, N 64, K = head dim), one thread issues
+        if (tid == 0) {
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+                const uint32_t qo = (uint32_t)((ks >> 2) * kTcBQ * 128 + (ks & 3) * 32);
+                const uint32_t ko = (uint32_t)((ks >> 2) * kTcBK * 128 + (ks & 3) * 32);
+                tc5::mma(t_s, tc5::desc_sw128(sbase + L::kOffQ + qo, 16, 1024),
+                         tc5::desc_sw128(sbase + L::kOffK + ko, 16, 1024), kIdescS, ks > 0);
+            }
+            tc5::commit(bar_s);
+        }
+        __syncwarp();
+        // S done implies every earlier MMA is done (commit tracks all prior
+        // ones): the K buffer, the other V buffer, P and O are free.
+        if (!mbar_wait_bounded(bar_s, (uint32_t)(kt & 1))) ok = false;
+        tc5::fence_after_sync();
+        // the next K (and, with two V buffers, the next V) start now
+        if (kt + 1 < nkt)
+            load_kv_tc<T, D, kSplit, true, !kSplit>(p, smem, sbase, buf ^ 1, kt + 1, c, kvh,
+                                                    kv_end);
+        cp_async_commit();
+
+        // ---- online softmax of this thread's row (base 2)
+        float sv[64];
+        {
+            float a[32], b2[32];
+            tc5::ld32(t_s + lane_base, a);
+            tc5::ld32(t_s + lane_base + 32, b2);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) { sv[j] = a[j]; sv[32 + j] = b2[j]; }
+        }
+        const uint8_t* okf = smem + L::kOffOk + (kt & 1) * kTcBK;
+        float mx = m_run;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+            const bool keep = okf[j] && kt * kTcBK + j <= qpos;
+            sv[j] = keep ? sv[j] * sl2 : -INFINITY;
+            mx = fmaxf(mx, sv[j]);
+        }
+        const float alpha = mx == -INFINITY ? 1.f : exp2f(m_run - mx);
+        float rs = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+            sv[j] = mx == -INFINITY ? 0.f : exp2f(sv[j] - mx);
+            rs += sv[j];
+        }
+        l_run = l_run * alpha + rs;
+        m_run = mx;
+        // ---- O *= alpha in tensor memory (warp-uniform: tcgen05.ld/st are
+        // warp-wide; rows that need no rescale multiply by 1)
+        if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += 32) {
+                float o[32];
+                tc5::ld32(t_o + lane_base + c0, o);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] *= alpha;
+                tc5::st32(t_o + lane_base + c0, o);
+            }
+        }
+        // ---- P (this row, 64 tokens) -> shared memory, K-major, swizzled
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            uint4 hi, lo;
+            split2<T>(sv[8 * u + 0], sv[8 * u + 1], hi.x, lo.x);
+            split2<T>(sv[8 * u + 2], sv[8 * u + 3], hi.y, lo.y);
+            split2<T>(sv[8 * u + 4], sv[8 * u + 5], hi.z, lo.z);
+            split2<T>(sv[8 * u + 6], sv[8 * u + 7], hi.w, lo.w);
+            *reinterpret_cast<uint4*>(smem + L::kOffP + sw128(row, u)) = hi;
+            if constexpr (kSplit)
+                *reinterpret_cast<uint4*>(smem + L::kOffP + L::kPTile + sw128(row, u)) = lo;
+        }
+        fence_proxy_async_smem();
+        tc5::fence_before_sync();
+        __syncthreads();
+        tc5::fence_after_sync();
+        // ---- O += P V (M 128, N = head dim, K 64 tokens; V MN-major)
+        const int vb = kSplit ? 0 : buf;
+        if (tid == 0) {
+#pragma unroll
+            for (int ks = 0; ks < kTcBK / 16; ++ks) {
+                const uint64_t bdesc = tc5::desc_sw128(
+                    sbase + L::kOffV + vb * L::kVBuf + ks * 16 * 128, kTcBK * 128, 1024);
+                tc5::mma(t_o, tc5::desc_sw128(sbase + L::kOffP + ks * 32, 16, 1024), bdesc,
+                         kIdescO, kt > 0 || ks > 0);
+                if constexpr (kSplit)
+                    tc5::mma(t_o, tc5::desc_sw128(sbase + L::kOffP + L::kPTile + ks * 32, 16, 1024),
+                             bdesc, kIdescO, true);
+            }
+            tc5::commit(bar_o);
+        }
+        __syncwarp();
+        if constexpr (kSplit) {
+            // one V buffer: the next V starts once this P V has read it
+            if (kt + 1 < nkt) {
+                if (!mbar_wait_bounded(bar_o, (uint32_t)(kt & 1))) ok = false;
+                tc5::fence_after_sync();
+                load_kv_tc<T, D, kSplit, false, true>(p, smem, sbase, 0, kt + 1, c, kvh, kv_end);
+            }
+            cp_async_commit();
+        }
+        // the next tile's K and V have landed and are visible to the tensor core
+        cp_async_wait<0>();
+        fence_proxy_async_smem();
+        __syncthreads();
+    }
 
     // ---- normalise and store (rows of the chunk only; an empty softmax -> 0)
     T* out = reinterpret_cast<T*>(p.out);
+    if (nkt > 0) {
+        if (!mbar_wait_bounded(bar_o, (uint32_t)((nkt - 1) & 1))) ok = false;
+        tc5::fence_after_sync();
+    }
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    T* dst = out + ((tok0 + row) * p.num_heads + h) * D;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const int row = r0 + 8 * r;
-        if (row >= rows_here) continue;
-        const float inv = l_run[r] > 0.f ? 1.f / l_run[r] : 0.f;
-        T* dst = out + ((tok0 + row) * p.num_heads + h) * D + 2 * q4;
+    for (int c0 = 0; c0 < D; c0 += 32) {
+        float o[32];
+        if (nkt > 0) {
+            tc5::ld32(t_o + lane_base + c0, o);
+        } else {
 #pragma unroll
-        for (int n = 0; n < NO; ++n) {
-            const uint32_t w = pack2<T>(o[n][2 * r] * inv, o[n][2 * r + 1] * inv);
-            *reinterpret_cast<uint32_t*>(dst + n * 8) = w;
+            for (int j = 0; j < 32; ++j) o[j] = 0.f;
+        }
+        if (row < rows_here) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint4 w;
+                w.x = pack2<T>(o[j + 0] * inv, o[j + 1] * inv);
+                w.y = pack2<T>(o[j + 2] * inv, o[j + 3] * inv);
+                w.z = pack2<T>(o[j + 4] * inv, o[j + 5] * inv);
+                w.w = pack2<T>(o[j + 6] * inv, o[j + 7] * inv);
+                *reinterpret_cast<uint4*>(dst + c0 + j) = w;
+            }
         }
     }
+    if (!ok && tid == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
+    tc5::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc5::dealloc(tmem, L::kTmemCols);
 }
 
 }  // namespace
@@ -308,13 +364,13 @@ bool supported(int dtype, int head_dim) {
 
 template <typename T, int D>
 cudaError_t launch_t(const Params& p, cudaStream_t st) {
-    using L = Layout<D>;
-    auto kern = prefill_attention_kernel<T, D>;
+    using L = TcLayout<D, !std::is_same<T, __half>::value>;
+    auto kern = prefill_attention_tc_kernel<T, D>;
     cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
     dim3 grid(p.q_tiles, p.num_heads, p.num_chunks);
-    kern<<<grid, kThreads, L::kBytes, st>>>(p);
+    kern<<<grid, kTcThreads, L::kAlloc, st>>>(p);
     return cudaGetLastError();
 }
 
@@ -342,7 +398,7 @@ cudaError_t launch_prefill_attention(int dtype, int head_dim, void* out, const v
     p.group = num_heads / num_kv_heads;
     p.block_size = block_size;
     p.max_blocks = max_blocks;
-    p.q_tiles = (max_query_len + prefill::kBQ - 1) / prefill::kBQ;
+    p.q_tiles = (max_query_len + prefill::kTcBQ - 1) / prefill::kTcBQ;
     p.scale_log2 = scale_log2;
     if (p.q_tiles == 0 || num_chunks == 0) return cudaSuccess;
     if (dtype == TLB_BFLOAT16)
