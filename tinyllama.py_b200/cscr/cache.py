@@ -18,6 +18,8 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
+
 import torch
 
 from . import _lib
@@ -33,12 +35,23 @@ def _block_bytes(cache: torch.Tensor) -> int:
 
 
 def _pairs_array(pairs):
+    """(src, dst) pairs as a ctypes int64 array (kept alive by the caller)."""
     n = len(pairs)
-    arr = (ctypes.c_int64 * (2 * max(n, 1)))()
-    for i, (s, d) in enumerate(pairs):
-        arr[2 * i] = s
-        arr[2 * i + 1] = d
-    return arr, n
+    arr = np.ascontiguousarray(np.asarray(pairs, dtype=np.int64).reshape(-1)) if n else \
+        np.zeros(2, np.int64)
+    return arr.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), n, arr
+
+
+def _check_mapping_range(block_mapping, nb: int, lo: int, hi: int) -> None:
+    """The reference's per-index range checks (cache.cpp:35-45), in its order;
+    the loop (and its message formatting) only runs when an index is out of
+    range."""
+    if lo >= 0 and hi < nb:
+        return
+    for s, dsts in block_mapping.items():
+        torch_check(0 <= int(s) < nb, f"src block index {int(s)} is out of range [0, {nb})")
+        for d in dsts:
+            torch_check(0 <= int(d) < nb, f"dst block index {int(d)} is out of range [0, {nb})")
 
 
 def swap_blocks(src: torch.Tensor, dst: torch.Tensor, block_mapping: dict[int, int]) -> None:
@@ -62,7 +75,7 @@ def swap_blocks(src: torch.Tensor, dst: torch.Tensor, block_mapping: dict[int, i
         torch_check(0 <= s < ns, f"src block index {s} is out of range [0, {ns})")
         torch_check(0 <= d < nd, f"dst block index {d} is out of range [0, {nd})")
         pairs.append((s, d))
-    arr, n = _pairs_array(pairs)
+    arr, n, _keep = _pairs_array(pairs)
     lib = _lib.load()
     if not src_cuda and not dst_cuda:
         _lib.check(lib.tlb_swap_blocks(src.data_ptr(), 0, dst.data_ptr(), 0, arr, n,
@@ -83,21 +96,19 @@ def copy_blocks(key_caches: list[torch.Tensor], value_caches: list[torch.Tensor]
     if not key_caches or not block_mapping:
         return
     device = key_caches[0].device
+    pairs = [(int(s), int(d)) for s, dsts in block_mapping.items() for d in dsts]
+    idx = [int(s) for s in block_mapping] + [d for _, d in pairs]
+    lo, hi = min(idx), max(idx)
     for cache in list(key_caches) + list(value_caches):
         torch_check(cache.is_cuda, "cache tensors must be CUDA tensors")
         torch_check(cache.device == device, "all cache tensors must be on the same GPU")
         torch_check(cache.dim() >= 1, "cache tensors must have at least one dimension")
         torch_check(cache.size(0) > 0, "cache tensors must contain at least one block")
         torch_check(cache.is_contiguous(), "cache tensors must be contiguous")
-        nb = cache.size(0)
-        for s, dsts in block_mapping.items():
-            torch_check(0 <= int(s) < nb, f"src block index {int(s)} is out of range [0, {nb})")
-            for d in dsts:
-                torch_check(0 <= int(d) < nb, f"dst block index {int(d)} is out of range [0, {nb})")
-    pairs = [(int(s), int(d)) for s, dsts in block_mapping.items() for d in dsts]
+        _check_mapping_range(block_mapping, cache.size(0), lo, hi)
     if not pairs:
         return
-    arr, n = _pairs_array(pairs)
+    arr, n, _keep = _pairs_array(pairs)
     # One launch per distinct block size (key and value caches normally agree).
     groups: dict[int, list[int]] = {}
     for cache in list(key_caches) + list(value_caches):
