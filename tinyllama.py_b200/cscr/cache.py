@@ -17,6 +17,7 @@
 from __future__ import annotations
 
 import ctypes
+import itertools
 
 import numpy as np
 
@@ -96,23 +97,30 @@ def copy_blocks(key_caches: list[torch.Tensor], value_caches: list[torch.Tensor]
     if not key_caches or not block_mapping:
         return
     device = key_caches[0].device
+    dev_index = key_caches[0].get_device()
     pairs = [(int(s), int(d)) for s, dsts in block_mapping.items() for d in dsts]
     idx = [int(s) for s in block_mapping] + [d for _, d in pairs]
     lo, hi = min(idx), max(idx)
-    for cache in list(key_caches) + list(value_caches):
+    # One pass over the caches: the reference's per-cache checks in its order
+    # (cache.cpp:48-105), then the cache's pointer into the group of its block
+    # size (one launch per distinct block size; key and value caches normally
+    # agree). A list of 72 caches costs ~1 us of Python per cache, so each
+    # tensor attribute is read once.
+    groups: dict[int, list[int]] = {}
+    for cache in itertools.chain(key_caches, value_caches):
         torch_check(cache.is_cuda, "cache tensors must be CUDA tensors")
-        torch_check(cache.device == device, "all cache tensors must be on the same GPU")
-        torch_check(cache.dim() >= 1, "cache tensors must have at least one dimension")
-        torch_check(cache.size(0) > 0, "cache tensors must contain at least one block")
+        torch_check(cache.get_device() == dev_index, "all cache tensors must be on the same GPU")
+        shape = cache.shape
+        torch_check(len(shape) >= 1, "cache tensors must have at least one dimension")
+        nb = shape[0]
+        torch_check(nb > 0, "cache tensors must contain at least one block")
         torch_check(cache.is_contiguous(), "cache tensors must be contiguous")
-        _check_mapping_range(block_mapping, cache.size(0), lo, hi)
+        _check_mapping_range(block_mapping, nb, lo, hi)
+        groups.setdefault(cache.element_size() * (cache.numel() // nb), []).append(
+            cache.data_ptr())
     if not pairs:
         return
     arr, n, _keep = _pairs_array(pairs)
-    # One launch per distinct block size (key and value caches normally agree).
-    groups: dict[int, list[int]] = {}
-    for cache in list(key_caches) + list(value_caches):
-        groups.setdefault(_block_bytes(cache), []).append(cache.data_ptr())
     lib = _lib.load()
     with _lib.device_guard(device):
         stream = _lib.stream_of(device)

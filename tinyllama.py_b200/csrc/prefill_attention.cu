@@ -65,8 +65,9 @@ struct Params {
     int num_kv_heads;
     int group;
     int block_size;
+    int bs_shift;                 // log2(block_size) when a power of two, else -1
     int max_blocks;
-    int q_tiles;                  // tiles of the longest chunk (gridDim.x)
+    int q_tiles;                  // tiles of the longest chunk (gridDim.z)
     float scale_log2;
 };
 
@@ -76,6 +77,7 @@ struct Params {
 constexpr int kTcBQ = 128;
 constexpr int kTcBK = 64;
 constexpr int kTcThreads = 128;
+constexpr float kRebase = 8.f;  // log2 units
 
 // With bf16 the probabilities go to the PV product as a hi + lo pair of bf16
 // values (16 significant bits, as in the decode kernel; bf16 alone keeps 8):
@@ -109,34 +111,64 @@ __device__ __forceinline__ uint32_t sw128(int row, int u) {
     return (uint32_t)(row * 128 + ((u ^ (row & 7)) << 4));
 }
 
-// KV tile `kt` (tokens kt*64 .. +63): K into the K buffer (and the usable
-// flag of every token into ok[kt % 2]), V into V buffer `vbuf`. Rows at or past
-// kv_end, or in a block whose id is negative or outside the pool, are
-// zero-filled and unusable.
+// Row split of a KV tile copy: a thread copies one 16-byte column unit of
+// kRows rows, kRowStep rows apart.
+template <int D>
+struct KvSplit {
+    static constexpr int kUnits = D / 8;                  // 16-byte units per row
+    static constexpr int kRowStep = kTcThreads / kUnits;  // rows between a thread's rows
+    static constexpr int kRows = kTcBK / kRowStep;        // rows per thread
+    static_assert(kTcThreads % kUnits == 0 && kTcBK % kRowStep == 0, "tile split");
+};
+
+// The block ids of this thread's rows of KV tile `kt` (-1 past kv_end). The
+// loads are issued back to back and consumed a stage later, so a tile's copies
+// do not wait on one table round trip per row.
+template <int D>
+__device__ __forceinline__ void fetch_blocks(const Params& p, int kt, int c, int kv_end,
+                                             int (&blk)[KvSplit<D>::kRows]) {
+    using S = KvSplit<D>;
+    const int* table = p.block_tables + (long long)c * p.max_blocks;
+    const int tok0 = kt * kTcBK + threadIdx.x / S::kUnits;
+#pragma unroll
+    for (int j = 0; j < S::kRows; ++j) {
+        const int tok = tok0 + j * S::kRowStep;
+        const int lb = p.bs_shift >= 0 ? tok >> p.bs_shift : tok / p.block_size;
+        blk[j] = tok < kv_end ? __ldg(table + lb) : -1;
+    }
+}
+
+// KV tile `kt` (tokens kt*64 .. +63) with its block ids `blk`: K into the K
+// buffer (and the usable flag of every token into ok[kt % 2]), V into V buffer
+// `vbuf`. Rows at or past kv_end, or in a block whose id is negative or
+// outside the pool, are zero-filled and unusable. Returns whether one of this
+// thread's rows below kv_end is unusable (the tile then needs the per-token
+// flags; otherwise token < kv_end says it all).
 template <typename T, int D, bool SPLIT, bool DO_K, bool DO_V>
-__device__ __forceinline__ void load_kv_tc(const Params& p, uint8_t* smem, uint32_t sbase,
-                                           int vbuf, int kt, int c, int kvh, int kv_end) {
+__device__ __forceinline__ bool load_kv_tc(const Params& p, uint8_t* smem, uint32_t sbase,
+                                           int vbuf, int kt, int kvh, int kv_end,
+                                           const int (&blk)[KvSplit<D>::kRows]) {
     using L = TcLayout<D, SPLIT>;
+    using S = KvSplit<D>;
     const T* kc = reinterpret_cast<const T*>(p.key_cache);
     const T* vc = reinterpret_cast<const T*>(p.value_cache);
-    const int* table = p.block_tables + (long long)c * p.max_blocks;
-    constexpr int kUnits = D / 8;  // 16-byte units per row
-    for (int i = threadIdx.x; i < kTcBK * kUnits; i += kTcThreads) {
-        const int row = i / kUnits, ua = i % kUnits;
+    const int ua = threadIdx.x % S::kUnits;
+    const int row0 = threadIdx.x / S::kUnits;
+    bool hole = false;
+#pragma unroll
+    for (int j = 0; j < S::kRows; ++j) {
+        const int row = row0 + j * S::kRowStep;
         const int tok = kt * kTcBK + row;
-        bool use = tok < kv_end;
+        bool use = blk[j] >= 0;
+        if (use && blk[j] >= p.num_blocks) {
+            use = false;
+            if (ua == 0 && DO_K) flag_status(TLB_STATUS_BAD_BLOCK_ID);
+        }
         long long off = 0;
         if (use) {
-            const int blk = table[tok / p.block_size];
-            if (blk < 0) {
-                use = false;
-            } else if (blk >= p.num_blocks) {
-                use = false;
-                if (ua == 0) flag_status(TLB_STATUS_BAD_BLOCK_ID);
-            } else {
-                off = (((long long)blk * p.num_kv_heads + kvh) * p.block_size +
-                       tok % p.block_size) * D + ua * 8;
-            }
+            const int in_blk = p.bs_shift >= 0 ? tok & (p.block_size - 1) : tok % p.block_size;
+            off = (((long long)blk[j] * p.num_kv_heads + kvh) * p.block_size + in_blk) * D +
+                  ua * 8;
         }
         const uint32_t dst = (uint32_t)((ua >> 3) * kTcBK * 128) + sw128(row, ua & 7);
         if (DO_K) {
@@ -144,7 +176,9 @@ __device__ __forceinline__ void load_kv_tc(const Params& p, uint8_t* smem, uint3
             if (ua == 0) smem[L::kOffOk + (kt & 1) * kTcBK + row] = use ? 1 : 0;
         }
         if (DO_V) cp_async_16(sbase + L::kOffV + vbuf * L::kVBuf + dst, vc + off, use);
+        hole |= !use && tok < kv_end;
     }
+    return hole;
 }
 
 template <typename T, int D>
@@ -162,9 +196,12 @@ __global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __ha
     const uint32_t bar_s = sbase + L::kOffBar, bar_o = bar_s + 8;
     const int tid = threadIdx.x, warp = tid >> 5;
 
-    const int c = blockIdx.z;
-    const int h = blockIdx.y;
-    const int tile = p.q_tiles - 1 - (int)blockIdx.x;  // late, heavier tiles first
+    // grid (heads, chunks, tiles): CTAs start in x, then y, then z order, so
+    // the late (heaviest) tiles of every chunk go first and the query heads of
+    // one kv head run side by side
+    const int h = blockIdx.x;
+    const int c = blockIdx.y;
+    const int tile = p.q_tiles - 1 - (int)blockIdx.z;
     const int q_begin = p.query_start[c];
     const int n_c = p.query_start[c + 1] - q_begin;
     if (tile * kTcBQ >= n_c) return;  // (also a chunk with no, or negative, length)
@@ -189,7 +226,14 @@ __global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __ha
         cp_async_16(sbase + L::kOffQ + (uint32_t)((ua >> 3) * kTcBQ * 128) + sw128(row, ua & 7),
                     src, use);
     }
-    if (nkt > 0) load_kv_tc<T, D, kSplit, true, true>(p, smem, sbase, 0, 0, c, kvh, kv_end);
+    constexpr int kRows = KvSplit<D>::kRows;
+    int blk[kRows], blk_next[kRows] = {};  // block ids of tiles kt + 1 and kt + 2
+    bool hole = false;
+    if (nkt > 0) {
+        fetch_blocks<D>(p, 0, c, kv_end, blk);
+        hole = load_kv_tc<T, D, kSplit, true, true>(p, smem, sbase, 0, 0, kvh, kv_end, blk);
+        fetch_blocks<D>(p, 1, c, kv_end, blk);
+    }
     cp_async_commit();
     if (tid == 0) {
         mbar_init(bar_s, 1);
@@ -200,7 +244,7 @@ __global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __ha
     cp_async_wait<0>();
     fence_proxy_async_smem();
     tc5::fence_before_sync();
-    __syncthreads();
+    int tile_holes = __syncthreads_or(hole);  // tile kt has unusable tokens below kv_end
     tc5::fence_after_sync();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::kOffSlot);
     const uint32_t t_s = tmem, t_o = tmem + kTcBK;          // columns of S and O
@@ -231,9 +275,12 @@ __global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __ha
         if (!mbar_wait_bounded(bar_s, (uint32_t)(kt & 1))) ok = false;
         tc5::fence_after_sync();
         // the next K (and, with two V buffers, the next V) start now
-        if (kt + 1 < nkt)
-            load_kv_tc<T, D, kSplit, true, !kSplit>(p, smem, sbase, buf ^ 1, kt + 1, c, kvh,
-                                                    kv_end);
+        hole = false;
+        if (kt + 1 < nkt) {
+            hole = load_kv_tc<T, D, kSplit, true, !kSplit>(p, smem, sbase, buf ^ 1, kt + 1, kvh,
+                                                           kv_end, blk);
+            fetch_blocks<D>(p, kt + 2, c, kv_end, blk_next);  // lands during the softmax
+        }
         cp_async_commit();
 
         // ---- online softmax of this thread's row (base 2)
@@ -245,23 +292,40 @@ __global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __ha
 #pragma unroll
             for (int j = 0; j < 32; ++j) { sv[j] = a[j]; sv[32 + j] = b2[j]; }
         }
-        const uint8_t* okf = smem + L::kOffOk + (kt & 1) * kTcBK;
-        float mx = m_run;
+        float mx = -INFINITY;
+        if (!tile_holes) {
+            // usable = below kv_end; causal = at or before this row's position
+            const int lim = min(qpos, kv_end - 1) - kt * kTcBK;
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-            const bool keep = okf[j] && kt * kTcBK + j <= qpos;
-            sv[j] = keep ? sv[j] * sl2 : -INFINITY;
-            mx = fmaxf(mx, sv[j]);
+            for (int j = 0; j < 64; ++j) {
+                sv[j] = j <= lim ? sv[j] * sl2 : -INFINITY;
+                mx = fmaxf(mx, sv[j]);
+            }
+        } else {
+            const uint8_t* okf = smem + L::kOffOk + (kt & 1) * kTcBK;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                const bool keep = okf[j] && kt * kTcBK + j <= qpos;
+                sv[j] = keep ? sv[j] * sl2 : -INFINITY;
+                mx = fmaxf(mx, sv[j]);
+            }
         }
-        const float alpha = mx == -INFINITY ? 1.f : exp2f(m_run - mx);
+        // The exponent base moves only when the row's maximum passes it by more
+        // than kRebase (a factor 2^8): probabilities then stay <= 256, exact
+        // to the storage type's relative precision, and O is rescaled on few
+        // tiles instead of on most of the early ones. The result is the same
+        // softmax (numerator and denominator share the base).
+        const bool rebase = mx > m_run + kRebase;
+        const float m_new = rebase ? mx : m_run;
+        const float alpha = rebase && m_run != -INFINITY ? exp2f(m_run - m_new) : 1.f;
         float rs = 0.f;
 #pragma unroll
         for (int j = 0; j < 64; ++j) {
-            sv[j] = mx == -INFINITY ? 0.f : exp2f(sv[j] - mx);
+            sv[j] = m_new == -INFINITY ? 0.f : exp2f(sv[j] - m_new);
             rs += sv[j];
         }
         l_run = l_run * alpha + rs;
-        m_run = mx;
+        m_run = m_new;
         // ---- O *= alpha in tensor memory (warp-uniform: tcgen05.ld/st are
         // warp-wide; rows that need no rescale multiply by 1)
         if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -311,14 +375,17 @@ __global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __ha
             if (kt + 1 < nkt) {
                 if (!mbar_wait_bounded(bar_o, (uint32_t)(kt & 1))) ok = false;
                 tc5::fence_after_sync();
-                load_kv_tc<T, D, kSplit, false, true>(p, smem, sbase, 0, kt + 1, c, kvh, kv_end);
+                load_kv_tc<T, D, kSplit, false, true>(p, smem, sbase, 0, kt + 1, kvh, kv_end,
+                                                      blk);
             }
             cp_async_commit();
         }
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) blk[j] = blk_next[j];
         // the next tile's K and V have landed and are visible to the tensor core
         cp_async_wait<0>();
         fence_proxy_async_smem();
-        __syncthreads();
+        tile_holes = __syncthreads_or(hole);
     }
 
     // ---- normalise and store (rows of the chunk only; an empty softmax -> 0)
@@ -369,7 +436,7 @@ cudaError_t launch_t(const Params& p, cudaStream_t st) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.q_tiles, p.num_heads, p.num_chunks);
+    dim3 grid(p.num_heads, p.num_chunks, p.q_tiles);
     kern<<<grid, kTcThreads, L::kAlloc, st>>>(p);
     return cudaGetLastError();
 }
@@ -397,6 +464,9 @@ cudaError_t launch_prefill_attention(int dtype, int head_dim, void* out, const v
     p.num_kv_heads = num_kv_heads;
     p.group = num_heads / num_kv_heads;
     p.block_size = block_size;
+    p.bs_shift = -1;
+    if (block_size > 0 && (block_size & (block_size - 1)) == 0)
+        p.bs_shift = __builtin_ctz((unsigned)block_size);
     p.max_blocks = max_blocks;
     p.q_tiles = (max_query_len + prefill::kTcBQ - 1) / prefill::kTcBQ;
     p.scale_log2 = scale_log2;
