@@ -103,6 +103,42 @@ def test_prompt_and_chunked_prefill_shapes(dtype, H, KVH, D, bs, built_lib):
     assert _lib.device_status() == 0
 
 
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("bs", [4, 24, 128, 192])
+def test_block_sizes_off_the_tma_tiling(dtype, bs, built_lib):
+    """Block sizes 4 and 24 take the kernel's cp.async loader (a TMA box of a
+    block would not tile a 64-token tile); 128 and 192 take TMA copies of a
+    64-row part of a block."""
+    chunk_lens = [1, 63, 64, 65, 200, 0, 100]
+    ctx_lens = [1, 63, 64, 65, 200, 10, 1000]
+    q, kc, vc, bt, qs, ctx = _chunks_case(chunk_lens, ctx_lens, 16, 2, 128, bs, dtype, seed=bs)
+    out = A.paged_prefill_attention(q, kc, vc, bt, qs, ctx, 128 ** -0.5)
+    torch.cuda.synchronize()
+    _check(q, kc, vc, bt, qs, ctx, 128 ** -0.5, dtype, out)
+    assert _lib.device_status() == 0
+
+
+def test_stale_nan_slots_past_the_context_never_leak(built_lib):
+    """Cache slots past each chunk's context (inside its last block) and the
+    whole of an unmapped block hold NaN: the output stays finite and matches
+    the oracle, which never reads them."""
+    chunk_lens, ctx_lens = [70, 33, 130], [70, 97, 130]
+    q, kc, vc, bt, qs, ctx = _chunks_case(chunk_lens, ctx_lens, 16, 2, 128, 16, "bfloat16",
+                                          seed=5)
+    for c, L in enumerate(ctx_lens):
+        last = int(bt[c, (L - 1) // 16])
+        kc[last, :, L % 16 or 16:] = float("nan")
+        vc[last, :, L % 16 or 16:] = float("nan")
+    spare = sorted(set(range(kc.shape[0])) - set(bt[bt >= 0].tolist()))
+    kc[spare] = float("nan")
+    vc[spare] = float("nan")
+    out = A.paged_prefill_attention(q, kc, vc, bt, qs, ctx, 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    _check(q, kc, vc, bt, qs, ctx, 128 ** -0.5, "bfloat16", out)
+    assert _lib.device_status() == 0
+
+
 def test_last_row_of_each_chunk_equals_decode_attention(built_lib):
     chunk_lens, ctx_lens = [300, 17, 1, 900], [300, 517, 4000, 900]
     q, kc, vc, bt, qs, ctx = _chunks_case(chunk_lens, ctx_lens, 16, 2, 128, 16, "bfloat16",

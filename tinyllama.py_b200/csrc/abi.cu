@@ -85,26 +85,33 @@ struct MapKey {
     uint64_t rows;
     int head_dim;
     int box_rows;
+    int box_chunks;
     bool operator==(const MapKey& o) const {
-        return ptr == o.ptr && rows == o.rows && head_dim == o.head_dim && box_rows == o.box_rows;
+        return ptr == o.ptr && rows == o.rows && head_dim == o.head_dim &&
+               box_rows == o.box_rows && box_chunks == o.box_chunks;
     }
 };
 struct MapKeyHash {
     size_t operator()(const MapKey& k) const {
         return std::hash<uintptr_t>()(k.ptr) ^ (std::hash<uint64_t>()(k.rows) * 31u) ^
-               ((size_t)k.head_dim << 20) ^ ((size_t)k.box_rows << 40);
+               ((size_t)k.head_dim << 20) ^ ((size_t)k.box_rows << 40) ^
+               ((size_t)k.box_chunks << 56);
     }
 };
 
 // A cache [rows = blocks * kv_heads * block_size, head_dim] of 16-bit elements
 // viewed as a 3-D tensor {64 columns, rows, head_dim / 64 column chunks}
-// (strides: a row, 128 bytes). One box = one (block, kv head) tile, stored in
-// shared memory chunk-major: [chunk][block_size rows][128 bytes], 128-byte
-// swizzle, so every 8-row group of a chunk is one 1024-byte swizzle atom.
-int kv_tensor_map(const void* base, uint64_t rows, int head_dim, int box_rows, CUtensorMap* out) {
+// (strides: a row, 128 bytes). A box holds box_rows rows of box_chunks chunks,
+// stored in shared memory chunk-major: [chunk][box_rows rows][128 bytes],
+// 128-byte swizzle, so every 8-row group of a chunk is one 1024-byte swizzle
+// atom. The decode kernel takes one (block, kv head) tile with every chunk per
+// box; the prefill kernel one chunk of it (its tiles keep a chunk's 64 rows
+// together).
+int kv_tensor_map(const void* base, uint64_t rows, int head_dim, int box_rows, int box_chunks,
+                  CUtensorMap* out) {
     static std::mutex mu;
     static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-    const MapKey key{reinterpret_cast<uintptr_t>(base), rows, head_dim, box_rows};
+    const MapKey key{reinterpret_cast<uintptr_t>(base), rows, head_dim, box_rows, box_chunks};
     {
         std::lock_guard<std::mutex> lk(mu);
         auto it = cache.find(key);
@@ -118,10 +125,50 @@ int kv_tensor_map(const void* base, uint64_t rows, int head_dim, int box_rows, C
     const cuuint32_t chunks = (cuuint32_t)(head_dim / 64);
     cuuint64_t dims[3] = {64, (cuuint64_t)rows, chunks};
     cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, 128};
-    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, chunks};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)box_chunks};
     cuuint32_t estr[3] = {1, 1, 1};
     CUtensorMap m;
     CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TLB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (cache.size() > 4096) cache.clear();
+        cache.emplace(key, m);
+    }
+    *out = m;
+    return TLB_OK;
+}
+
+// The same cache viewed as a 4-D tensor {64 columns, 8 rows, head_dim / 64
+// chunks, rows / 8 groups of 8 rows} (strides: a row, 128 bytes, 8 rows): a
+// box {64, 8, chunks, box_rows / 8} holds box_rows rows with every chunk,
+// stored [8-row group][chunk][8 rows][128 bytes] with 128-byte swizzle (the
+// prefill kernel's K / V tiles: one stride between 8-row groups whichever
+// block they come from). rows and box_rows are multiples of 8.
+int kv_group_tensor_map(const void* base, uint64_t rows, int head_dim, int box_rows,
+                        CUtensorMap* out) {
+    static std::mutex mu;
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{reinterpret_cast<uintptr_t>(base), rows, head_dim, box_rows, -1};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return TLB_OK;
+        }
+    }
+    auto fn = encode_fn();
+    if (fn == nullptr) return fail(TLB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    const cuuint32_t chunks = (cuuint32_t)(head_dim / 64);
+    cuuint64_t dims[4] = {64, 8, chunks, (cuuint64_t)(rows / 8)};
+    cuuint64_t strides[3] = {(cuuint64_t)head_dim * 2, 128, (cuuint64_t)head_dim * 2 * 8};
+    cuuint32_t box[4] = {64, 8, chunks, (cuuint32_t)(box_rows / 8)};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUtensorMap m;
+    CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides,
                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(TLB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -220,11 +267,25 @@ int tlb_paged_prefill_attention(void* out, const void* query, const void* key_ca
     TLB_REQUIRE(aligned(out, 16) && aligned(query, 16) && aligned(key_cache, 16) &&
                     aligned(value_cache, 16),
                 "query, out and the caches must be 16-byte aligned");
+    // K and V tiles by TMA where a box can tile the blocks and every cache row
+    // has a 32-bit coordinate; otherwise the kernel's cp.async loader
+    CUtensorMap tk, tv;
+    const CUtensorMap *ptk = nullptr, *ptv = nullptr;
+    const int box_rows = tlb::prefill_box_rows((int)block_size);
+    const long long rows = num_blocks * num_kv_heads * block_size;
+    if (box_rows > 0 && rows < (1ll << 31) && num_blocks < (1ll << 31)) {
+        if (int rc = kv_group_tensor_map(key_cache, (uint64_t)rows, (int)head_dim, box_rows, &tk))
+            return rc;
+        if (int rc = kv_group_tensor_map(value_cache, (uint64_t)rows, (int)head_dim, box_rows, &tv))
+            return rc;
+        ptk = &tk;
+        ptv = &tv;
+    }
     cudaError_t e = tlb::launch_prefill_attention(
         dtype, (int)head_dim, out, query, key_cache, value_cache, block_tables, query_start,
         context_lens, num_blocks, (int)num_chunks, (int)num_heads, (int)num_kv_heads,
         (int)block_size, (int)max_blocks_per_seq, (int)max_query_len,
-        scale * 1.4426950408889634f, reinterpret_cast<cudaStream_t>(stream));
+        scale * 1.4426950408889634f, ptk, ptv, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "launching prefill attention");
     return TLB_OK;
 }
@@ -351,8 +412,11 @@ int attention_impl(void* out, const void* query, const void* key_cache,
                         "paged_attention needs a 256-byte aligned workspace of %zu bytes (got %zu)",
                         w.total, workspace_bytes);
         CUtensorMap tk, tv;
-        if (int rc = kv_tensor_map(key_cache, rows, (int)head_dim, (int)block_size, &tk)) return rc;
-        if (int rc = kv_tensor_map(value_cache, rows, (int)head_dim, (int)block_size, &tv)) return rc;
+        const int chunks = (int)head_dim / 64;
+        if (int rc = kv_tensor_map(key_cache, rows, (int)head_dim, (int)block_size, chunks, &tk))
+            return rc;
+        if (int rc = kv_tensor_map(value_cache, rows, (int)head_dim, (int)block_size, chunks, &tv))
+            return rc;
         tlb::attn::TcParams p{};
         char* ws = static_cast<char*>(workspace);
         p.out = out;

@@ -173,7 +173,11 @@ cudaError_t launch_prefill_attention(int dtype, int head_dim, void* out, const v
                                      const int32_t* context_lens, long long num_blocks,
                                      int num_chunks, int num_heads, int num_kv_heads,
                                      int block_size, int max_blocks, int max_query_len,
-                                     float scale_log2, cudaStream_t stream);
+                                     float scale_log2, const CUtensorMap* tm_k,
+                                     const CUtensorMap* tm_v, cudaStream_t stream);
+// Cache rows per TMA copy of the prefill kernel for this block size (a block,
+// or a 64-row part of one), 0 when the block size needs the cp.async loader.
+int prefill_box_rows(int block_size);
 
 // ------------------------------------------------------------ block copies
 constexpr int kCopyMaxCaches = 128;
