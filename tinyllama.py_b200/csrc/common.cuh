@@ -46,7 +46,8 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Probabilities in [0, 1] as mma operands: fp16 keeps 11 significant bits,
+// Probabilities as mma operands (in [0, 1] in the decode kernel, at most 2^8
+// with the prefill kernel's lazy exponent base): fp16 keeps 11 significant bits,
 // which is enough; bf16 keeps 8, so it is carried as a hi + lo pair whose sum
 // holds 16 bits (lo is the bf16 rounding of the remainder).
 template <typename T> constexpr bool kSplitP = false;

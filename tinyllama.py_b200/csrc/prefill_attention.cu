@@ -319,18 +319,6 @@ __device__ __forceinline__ void softmax_tile(uint8_t* smem_p, const uint8_t* okf
     const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
     l_run = l_run * alpha + rs;
     m_run = m_new;
-    // ---- O *= alpha in tensor memory (warp-uniform: tcgen05.ld/st are
-    // warp-wide; rows that need no rescale multiply by 1)
-    if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-            float o[32];
-            tc5::ld32(t_o + c0, o);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] *= alpha;
-            tc5::st32(t_o + c0, o);
-        }
-    }
     // ---- P (this row, 64 tokens) -> shared memory, K-major, swizzled
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -342,6 +330,19 @@ __device__ __forceinline__ void softmax_tile(uint8_t* smem_p, const uint8_t* okf
         *reinterpret_cast<uint4*>(smem_p + sw128(row, u)) = hi;
         if constexpr (SPLIT)
             *reinterpret_cast<uint4*>(smem_p + kTcBQ * 128 + sw128(row, u)) = lo;
+    }
+    // ---- O *= alpha in tensor memory, after P is out of registers (warp-
+    // uniform: tcgen05.ld/st are warp-wide; rows that need no rescale
+    // multiply by 1)
+    if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+            float o[32];
+            tc5::ld32(t_o + c0, o);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] *= alpha;
+            tc5::st32(t_o + c0, o);
+        }
     }
 }
 
@@ -524,12 +525,106 @@ __global__ void __launch_bounds__(kTcThreads, (D == 128 || !std::is_same<T, __ha
     if (warp == 0) tc5::dealloc(tmem, L::kTmemCols);
 }
 
+// Shared-memory layout of the warp-specialised kernel: Q, two K and two V
+// buffers (P lives in tensor memory), usable flags and unmapped-block flags of
+// four tiles in flight, mbarriers.
+template <int D>
+struct WsLayout {
+    static constexpr int kCh = D / 64;
+    static constexpr int kKV = kCh * kTcBK * 128;                // one K or V tile
+    static constexpr int kOffQ = 0;                              // [kCh][128 rows][128 B]
+    static constexpr int kOffK = kOffQ + kCh * kTcBQ * 128;      // 2 x [8 groups][kCh][8][128 B]
+    static constexpr int kOffV = kOffK + 2 * kKV;                // 2 x the same
+    static constexpr int kOffOk = kOffV + 2 * kKV;               // [4][64] token usable
+    static constexpr int kOffHole = kOffOk + 4 * kTcBK;          // [4] tile has unmapped blocks
+    // mbarriers: S done [2], O done [2] (per S / V buffer), K landed [2], V landed [2]
+    static constexpr int kOffBar = kOffHole + 16;
+    static constexpr int kOffSlot = kOffBar + 64;                // tensor-memory address
+    static constexpr int kBytes = kOffSlot + 16;
+    static constexpr int kAlloc = kBytes + 1024;                 // slack for 1024-byte alignment
+    // tensor memory: S / P of tiles kt and kt + 1 (64 columns each), then O
+    static constexpr uint32_t kTmemCols = 256;
+    static_assert(2 * kTcBK + D <= (int)kTmemCols, "S, S and O fit the allocation");
+    static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kKV % 1024 == 0,
+                  "swizzled tiles on 1024-byte boundaries");
+};
+
+// Online softmax (base 2) of KV tile `kt` for this thread's query row, with P
+// kept in tensor memory: reads the row's S (columns t_s..t_s+63 of its lane),
+// keeps the usable tokens at or before the row's position, updates the
+// running (m_run, l_run) and writes the row's probabilities over its S:
+// columns t_s..t_s+31 hold 64 values packed in pairs (with SPLIT the high
+// parts there and the low parts in t_s+32..t_s+63). Returns the factor the
+// row of O must be scaled by before this tile's P V.
+template <typename T, bool SPLIT>
+__device__ __forceinline__ float softmax_tile_tm(const uint8_t* okf, bool holes, uint32_t t_s,
+                                                 int kt, int qpos, int kv_end, float sl2,
+                                                 float& m_run, float& l_run) {
+    float sv[64];
+    {
+        float a[32], b2[32];
+        tc5::ld32(t_s, a);
+        tc5::ld32(t_s + 32, b2);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) { sv[j] = a[j]; sv[32 + j] = b2[j]; }
+    }
+    // row maximum and (below) row sum as eight interleaved partials
+    float mx8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+    if (!holes) {
+        // usable = below kv_end; causal = at or before this row's position
+        const int lim = min(qpos, kv_end - 1) - kt * kTcBK;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+            sv[j] = j <= lim ? sv[j] * sl2 : -INFINITY;
+            mx8[j & 7] = fmaxf(mx8[j & 7], sv[j]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+            const bool keep = okf[j] && kt * kTcBK + j <= qpos;
+            sv[j] = keep ? sv[j] * sl2 : -INFINITY;
+            mx8[j & 7] = fmaxf(mx8[j & 7], sv[j]);
+        }
+    }
+    const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+    // lazy exponent base (see softmax_tile)
+    const bool rebase = mx > m_run + kRebase;
+    const float m_new = rebase ? mx : m_run;
+    const float alpha = rebase && m_run != -INFINITY ? exp2f(m_run - m_new) : 1.f;
+    float rs8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+        sv[j] = m_new == -INFINITY ? 0.f : exp2f(sv[j] - m_new);
+        rs8[j & 7] += sv[j];
+    }
+    const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+    l_run = l_run * alpha + rs;
+    m_run = m_new;
+    uint32_t ph[32], pl[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) split2<T>(sv[2 * j], sv[2 * j + 1], ph[j], pl[j]);
+    tc5::st32u(t_s, ph);
+    if constexpr (SPLIT) tc5::st32u(t_s + 32, pl);
+    return alpha;
+}
+
 // ---------------------------------------------------------------- warp-specialised
 // Warps 0-3 run the softmax of the CTA's 128 query rows (thread 0 also issues
-// the MMAs); warp 4 only issues the TMA copies of K and V, so no copy issue
-// sits inside the softmax warps' per-tile barrier. K is single-buffered (K
-// of tile kt goes in once S of tile kt - 1 has completed), V double-buffered
-// with fp16 and single-buffered with bf16 (whose P takes two tiles).
+// the MMAs); warp 4 only issues the TMA copies of K and V. S is
+// double-buffered in tensor memory and P is written over its own S, so the
+// tensor core runs P V of tile kt - 1 and S of tile kt + 1 while the softmax
+// warps work on tile kt:
+//   thread 0, end of iteration kt: P V (kt) -> O, then S (kt + 2) -> S buffer
+//   kt % 2 (issued in order: the P V read of that buffer comes first);
+//   copy warp: K (kt) into K buffer kt % 2 once S (kt - 2) is done, V (kt)
+//   into V buffer kt % 2 once P V (kt - 2) is done.
+// Every mbarrier is per buffer, so none can complete a second phase before
+// its waiters have seen the first.
 constexpr int kWsThreads = kTcThreads + 32;
 
 __device__ __forceinline__ void softmax_warps_sync() {
@@ -543,7 +638,7 @@ __global__ void __launch_bounds__(kWsThreads, 2)
     constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
     constexpr bool kSplit = kBf16;  // P as a hi + lo pair of bf16
     constexpr int kCh = D / 64;
-    using L = TcLayout<D, kSplit>;
+    using L = WsLayout<D>;
     constexpr uint32_t kIdescS = tc5::idesc_f16(kBf16, false, kTcBQ, kTcBK);
     constexpr uint32_t kIdescO = tc5::idesc_f16(kBf16, true, kTcBQ, D);
     constexpr uint32_t kGroupStride = kCh * 1024;  // bytes between 8-token groups of K / V
@@ -551,9 +646,9 @@ __global__ void __launch_bounds__(kWsThreads, 2)
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_s = sbase + L::kOffBar, bar_o = bar_s + 8, bar_k = bar_s + 16;
-    const uint32_t bar_v0 = bar_s + 24;  // V buffer b: bar_v0 + 8 b
-    const uint32_t bar_kseen = bar_s + 40;
+    // buffer b: bar_s + 8 b, bar_o + 8 b, bar_k + 8 b, bar_v + 8 b
+    const uint32_t bar_s = sbase + L::kOffBar, bar_o = bar_s + 16, bar_k = bar_s + 32,
+                   bar_v = bar_s + 48;
     volatile int* hflag = reinterpret_cast<volatile int*>(smem + L::kOffHole);
     const int tid = threadIdx.x, warp = tid >> 5;
 
@@ -576,12 +671,7 @@ __global__ void __launch_bounds__(kWsThreads, 2)
     const int nkt = (kv_end + kTcBK - 1) / kTcBK;
 
     if (tid == 0) {
-        mbar_init(bar_s, 1);
-        mbar_init(bar_o, 1);
-        mbar_init(bar_k, 1);
-        mbar_init(bar_v0, 1);
-        mbar_init(bar_v0 + 8, 1);
-        mbar_init(bar_kseen, kTcThreads / 32);
+        for (int i = 0; i < 8; ++i) mbar_init(bar_s + 8 * i, 1);
         fence_mbar_init();
     }
     if (tid == kTcThreads) {
@@ -616,115 +706,123 @@ __global__ void __launch_bounds__(kWsThreads, 2)
         // ======================================================== copy warp
         int blk = tma_block_of(p, 0, c, kv_end);
         for (int kt = 0; kt < nkt; ++kt) {
+            const int b = kt & 1;
+            const uint32_t prev = (uint32_t)(((kt - 2) >> 1) & 1);  // phase of tile kt - 2
             const int blk_next = tma_block_of(p, kt + 1, c, kv_end);  // lands while waiting
-            // K buffer (and, with two V buffers, this tile's V buffer) free:
-            // S of tile kt - 1 done, which implies every earlier MMA is. And
-            // every softmax warp has seen K of tile kt - 1 land, so the K
-            // barrier never runs two phases ahead of a warp that waits on it.
-            if (kt > 0) {
-                if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar_s, (uint32_t)((kt - 1) & 1))))
-                    ok = false;
-                if (!__all_sync(0xffffffffu,
-                                mbar_wait_bounded(bar_kseen, (uint32_t)((kt - 1) & 1))))
-                    ok = false;
-            }
+            // K buffer b is free once S of tile kt - 2 is done
+            if (kt >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(bar_s + 8 * b, prev)))
+                ok = false;
             const bool hole =
-                tile_flags_ws(p, smem + L::kOffOk + (kt & 1) * kTcBK, kt, kv_end, blk);
+                tile_flags_ws(p, smem + L::kOffOk + (kt & 3) * kTcBK, kt, kv_end, blk);
             const bool any_hole = __any_sync(0xffffffffu, hole);
-            if ((tid & 31) == 0) hflag[kt & 1] = any_hole ? 1 : 0;
+            if ((tid & 31) == 0) hflag[kt & 3] = any_hole ? 1 : 0;
             __syncwarp();  // flags stored before lane 0's arrive (release) below
-            issue_kv_ws<D>(p, &tm_k, sbase + L::kOffK, bar_k, kt, kvh, blk);
-            if constexpr (kSplit) {
-                // one V buffer: free once P V of tile kt - 1 has read it
-                if (kt > 0 &&
-                    !__all_sync(0xffffffffu, mbar_wait_bounded(bar_o, (uint32_t)((kt - 1) & 1))))
-                    ok = false;
-                issue_kv_ws<D>(p, &tm_v, sbase + L::kOffV, bar_v0, kt, kvh, blk);
-            } else {
-                issue_kv_ws<D>(p, &tm_v, sbase + L::kOffV + (kt & 1) * L::kVBuf,
-                               bar_v0 + 8 * (kt & 1), kt, kvh, blk);
-            }
+            issue_kv_ws<D>(p, &tm_k, sbase + L::kOffK + b * L::kKV, bar_k + 8 * b, kt, kvh, blk);
+            // V buffer b is free once P V of tile kt - 2 is done
+            if (kt >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(bar_o + 8 * b, prev)))
+                ok = false;
+            issue_kv_ws<D>(p, &tm_v, sbase + L::kOffV + b * L::kKV, bar_v + 8 * b, kt, kvh, blk);
             blk = blk_next;
         }
     } else {
         // ===================================================== softmax warps
-        const uint32_t t_s = tmem, t_o = tmem + kTcBK;          // columns of S and O
+        const uint32_t t_o = tmem + 2 * kTcBK;                   // columns of O
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;  // this warp's lanes
         const int row = tid;  // query row of this thread
         const int qpos = first_pos + tile * kTcBQ + row;
         const float sl2 = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;
+        // S = Q K^T of tile j (M 128, N 64, K = head dim) into S buffer j % 2,
+        // once K of tile j has landed (thread 0)
+        auto issue_s = [&](int j) {
+            const int b = j & 1;
+            if (!mbar_wait_bounded(bar_k + 8 * b, (uint32_t)((j >> 1) & 1))) ok = false;
+            tc5::fence_after_sync();
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+                const uint32_t qo = (uint32_t)((ks >> 2) * kTcBQ * 128 + (ks & 3) * 32);
+                const uint32_t ko = (uint32_t)(b * L::kKV + (ks >> 2) * 1024 + (ks & 3) * 32);
+                tc5::mma(tmem + b * kTcBK, tc5::desc_sw128(sbase + L::kOffQ + qo, 16, 1024),
+                         tc5::desc_sw128(sbase + L::kOffK + ko, 16, kGroupStride), kIdescS,
+                         ks > 0);
+            }
+            tc5::commit(bar_s + 8 * b);
+        };
+        if (tid == 0) {
+            for (int j = 0; j < min(2, nkt); ++j) issue_s(j);
+        }
+        // thread 0 has seen K of tiles 0 and 1 land: their flags are visible
+        // to every softmax thread past this barrier (and those of tile kt + 2,
+        // seen at the end of iteration kt, past the barrier of iteration kt + 1)
+        softmax_warps_sync();
         for (int kt = 0; kt < nkt; ++kt) {
-            const int vb = kSplit ? 0 : (kt & 1);
-            const uint32_t v_parity = (uint32_t)(kSplit ? (kt & 1) : ((kt >> 1) & 1));
-            // K of this tile has landed; its flags were stored before
-            if (!mbar_wait_bounded(bar_k, (uint32_t)(kt & 1))) ok = false;
-            const bool holes = hflag[kt & 1] != 0;
-            __syncwarp();
-            if ((tid & 31) == 0) mbar_arrive(bar_kseen);
-            // ---- S = Q K^T (M 128, N 64, K = head dim), one thread issues
-            if (tid == 0) {
+            const int b = kt & 1;
+            const uint32_t par = (uint32_t)((kt >> 1) & 1);  // phase of tile kt on buffer b
+            const bool holes = hflag[kt & 3] != 0;
+            const uint8_t* okf = smem + L::kOffOk + (kt & 3) * kTcBK;
+            if (!mbar_wait_bounded(bar_s + 8 * b, par)) ok = false;
+            tc5::fence_after_sync();
+            const float alpha = softmax_tile_tm<T, kSplit>(okf, holes, tmem + b * kTcBK + lane_base,
+                                                           kt, qpos, kv_end, sl2, m_run, l_run);
+            // ---- O *= alpha (rare with the lazy base), once P V of tile
+            // kt - 1 has accumulated into it (warp-uniform: tcgen05.ld/st are
+            // warp-wide; rows that need no rescale multiply by 1)
+            if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                if (!mbar_wait_bounded(bar_o + 8 * (b ^ 1), (uint32_t)(((kt - 1) >> 1) & 1)))
+                    ok = false;
                 tc5::fence_after_sync();
 #pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t qo = (uint32_t)((ks >> 2) * kTcBQ * 128 + (ks & 3) * 32);
-                    const uint32_t ko = (uint32_t)((ks >> 2) * 1024 + (ks & 3) * 32);
-                    tc5::mma(t_s, tc5::desc_sw128(sbase + L::kOffQ + qo, 16, 1024),
-                             tc5::desc_sw128(sbase + L::kOffK + ko, 16, kGroupStride), kIdescS,
-                             ks > 0);
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tc5::ld32(t_o + lane_base + c0, o);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] *= alpha;
+                    tc5::st32(t_o + lane_base + c0, o);
                 }
-                tc5::commit(bar_s);
             }
-            __syncwarp();
-            if (!mbar_wait_bounded(bar_s, (uint32_t)(kt & 1))) ok = false;
-            tc5::fence_after_sync();
-            softmax_tile<T, D, kSplit>(smem + L::kOffP, smem + L::kOffOk + (kt & 1) * kTcBK,
-                                       holes, t_s + lane_base, t_o + lane_base, kt, row, qpos,
-                                       kv_end, sl2, m_run, l_run);
             // A box moves whole blocks: V rows past the context, or of an
             // unmapped block (never copied: stale shared memory), are zeroed
             // once the tile's V has landed, so 0 x (stale NaN) never reaches O.
             bool v_waited = false;
             if (holes || (kt == nkt - 1 && kv_end - kt * kTcBK < kTcBK)) {
-                if (!mbar_wait_bounded(bar_v0 + 8 * vb, v_parity)) ok = false;
+                if (!mbar_wait_bounded(bar_v + 8 * b, par)) ok = false;
                 v_waited = true;
-                const uint8_t* okf = smem + L::kOffOk + (kt & 1) * kTcBK;
                 for (int i = tid; i < kTcBK * kCh * 8; i += kTcThreads) {
                     const int r = i / (kCh * 8), u = i % (kCh * 8);
                     if (!okf[r])
-                        *reinterpret_cast<uint4*>(smem + L::kOffV + vb * L::kVBuf +
+                        *reinterpret_cast<uint4*>(smem + L::kOffV + b * L::kKV +
                                                   (r >> 3) * kGroupStride + (u >> 3) * 1024 +
                                                   (r & 7) * 128 + (u & 7) * 16) =
                             make_uint4(0u, 0u, 0u, 0u);
                 }
+                fence_proxy_async_smem();
             }
-            fence_proxy_async_smem();
             tc5::fence_before_sync();
             softmax_warps_sync();
             tc5::fence_after_sync();
-            // ---- O += P V (M 128, N = head dim, K 64 tokens; V MN-major)
             if (tid == 0) {
-                if (!v_waited && !mbar_wait_bounded(bar_v0 + 8 * vb, v_parity)) ok = false;
+                // ---- O += P V (M 128, N = head dim, K 64 tokens; P from tensor
+                // memory, V MN-major from shared memory)
+                if (!v_waited && !mbar_wait_bounded(bar_v + 8 * b, par)) ok = false;
+                tc5::fence_after_sync();
 #pragma unroll
                 for (int ks = 0; ks < kTcBK / 16; ++ks) {
                     const uint64_t bdesc = tc5::desc_sw128(
-                        sbase + L::kOffV + vb * L::kVBuf + ks * 2 * kGroupStride, 1024,
-                        kGroupStride);
-                    tc5::mma(t_o, tc5::desc_sw128(sbase + L::kOffP + ks * 32, 16, 1024), bdesc,
-                             kIdescO, kt > 0 || ks > 0);
+                        sbase + L::kOffV + b * L::kKV + ks * 2 * kGroupStride, 1024, kGroupStride);
+                    tc5::mma_ts(t_o, tmem + b * kTcBK + ks * 8, bdesc, kIdescO, kt > 0 || ks > 0);
                     if constexpr (kSplit)
-                        tc5::mma(t_o,
-                                 tc5::desc_sw128(sbase + L::kOffP + L::kPTile + ks * 32, 16, 1024),
-                                 bdesc, kIdescO, true);
+                        tc5::mma_ts(t_o, tmem + b * kTcBK + 32 + ks * 8, bdesc, kIdescO, true);
                 }
-                tc5::commit(bar_o);
+                tc5::commit(bar_o + 8 * b);
+                if (kt + 2 < nkt) issue_s(kt + 2);
             }
             __syncwarp();
         }
         // ---- normalise and store (rows of the chunk only; an empty softmax -> 0)
         T* out = reinterpret_cast<T*>(p.out);
         if (nkt > 0) {
-            if (!mbar_wait_bounded(bar_o, (uint32_t)((nkt - 1) & 1))) ok = false;
+            const int last = nkt - 1;
+            if (!mbar_wait_bounded(bar_o + 8 * (last & 1), (uint32_t)((last >> 1) & 1))) ok = false;
             tc5::fence_after_sync();
         }
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -754,7 +852,7 @@ __global__ void __launch_bounds__(kWsThreads, 2)
     if (!ok) flag_status(TLB_STATUS_WAIT_TIMEOUT);
     tc5::fence_before_sync();
     __syncthreads();
-    if (warp == 0) tc5::dealloc(tmem, L::kTmemCols);
+    if (warp == 0) tc5::dealloc(tmem, WsLayout<D>::kTmemCols);
 }
 
 }  // namespace
@@ -769,11 +867,12 @@ cudaError_t launch_d(const Params& p, const CUtensorMap* tk, const CUtensorMap* 
     using L = TcLayout<D, !std::is_same<T, __half>::value>;
     const dim3 grid(p.num_heads, p.num_chunks, p.q_tiles);
     if (tk != nullptr && tv != nullptr) {
+        constexpr int kAlloc = WsLayout<D>::kAlloc;
         auto kern = prefill_attention_ws_kernel<T, D>;
         cudaError_t e =
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAlloc);
         if (e != cudaSuccess) return e;
-        kern<<<grid, kWsThreads, L::kAlloc, st>>>(*tk, *tv, p);
+        kern<<<grid, kWsThreads, kAlloc, st>>>(*tk, *tv, p);
     } else {
         auto kern = prefill_attention_tc_kernel<T, D>;
         cudaError_t e =
