@@ -537,9 +537,10 @@ struct WsLayout {
     static constexpr int kOffV = kOffK + 2 * kKV;                // 2 x the same
     static constexpr int kOffOk = kOffV + 2 * kKV;               // [4][64] token usable
     static constexpr int kOffHole = kOffOk + 4 * kTcBK;          // [4] tile has unmapped blocks
-    // mbarriers: S done [2], O done [2] (per S / V buffer), K landed [2], V landed [2]
+    // mbarriers: S done [2], O done [2] (per S / V buffer), K landed [2], V landed [2],
+    // P ready [2] (per S buffer), flags stored [4] (per flag slot)
     static constexpr int kOffBar = kOffHole + 16;
-    static constexpr int kOffSlot = kOffBar + 64;                // tensor-memory address
+    static constexpr int kOffSlot = kOffBar + 112;               // tensor-memory address
     static constexpr int kBytes = kOffSlot + 16;
     static constexpr int kAlloc = kBytes + 1024;                 // slack for 1024-byte alignment
     // tensor memory: S / P of tiles kt and kt + 1 (64 columns each), then O
@@ -614,22 +615,21 @@ __device__ __forceinline__ float softmax_tile_tm(const uint8_t* okf, bool holes,
 }
 
 // ---------------------------------------------------------------- warp-specialised
-// Warps 0-3 run the softmax of the CTA's 128 query rows (thread 0 also issues
-// the MMAs); warp 4 only issues the TMA copies of K and V. S is
-// double-buffered in tensor memory and P is written over its own S, so the
-// tensor core runs P V of tile kt - 1 and S of tile kt + 1 while the softmax
-// warps work on tile kt:
-//   thread 0, end of iteration kt: P V (kt) -> O, then S (kt + 2) -> S buffer
-//   kt % 2 (issued in order: the P V read of that buffer comes first);
-//   copy warp: K (kt) into K buffer kt % 2 once S (kt - 2) is done, V (kt)
-//   into V buffer kt % 2 once P V (kt - 2) is done.
-// Every mbarrier is per buffer, so none can complete a second phase before
-// its waiters have seen the first.
-constexpr int kWsThreads = kTcThreads + 32;
-
-__device__ __forceinline__ void softmax_warps_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kTcThreads) : "memory");
-}
+// Warps 0-3 run the softmax of the CTA's 128 query rows; warp 4 issues the
+// TMA copies of K and V, warp 5 the MMAs. S is double-buffered in tensor
+// memory and P is written over its own S, so the tensor core runs P V of
+// tile kt - 1 and S of tile kt + 1 while the softmax warps work on tile kt:
+//   MMA warp: once every softmax warp has put P (kt) in place, P V (kt) -> O,
+//   then S (kt + 2) -> S buffer kt % 2 (issued in order: the P V read of that
+//   buffer comes first);
+//   copy warp: K (kt) into K buffer kt % 2 once S (kt - 2) is done, then the
+//   tile's usable flags into flag slot kt % 4, V (kt) into V buffer kt % 2
+//   once P V (kt - 2) is done.
+// The softmax warps never wait for one another. Every mbarrier is per buffer
+// or per slot, so none can complete a second phase before its waiters have
+// seen the first.
+constexpr int kWsThreads = kTcThreads + 64;
+constexpr int kCopyWarp = kTcThreads / 32, kMmaWarp = kCopyWarp + 1;
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kWsThreads, 2)
@@ -646,9 +646,10 @@ __global__ void __launch_bounds__(kWsThreads, 2)
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     const uint32_t sbase = smem_u32(smem);
-    // buffer b: bar_s + 8 b, bar_o + 8 b, bar_k + 8 b, bar_v + 8 b
+    // buffer b: bar_s + 8 b, bar_o + 8 b, bar_k + 8 b, bar_v + 8 b, bar_p + 8 b;
+    // flag slot f: bar_f + 8 f
     const uint32_t bar_s = sbase + L::kOffBar, bar_o = bar_s + 16, bar_k = bar_s + 32,
-                   bar_v = bar_s + 48;
+                   bar_v = bar_s + 48, bar_p = bar_s + 64, bar_f = bar_s + 80;
     volatile int* hflag = reinterpret_cast<volatile int*>(smem + L::kOffHole);
     const int tid = threadIdx.x, warp = tid >> 5;
 
@@ -672,6 +673,9 @@ __global__ void __launch_bounds__(kWsThreads, 2)
 
     if (tid == 0) {
         for (int i = 0; i < 8; ++i) mbar_init(bar_s + 8 * i, 1);
+        mbar_init(bar_p, kTcThreads / 32);
+        mbar_init(bar_p + 8, kTcThreads / 32);
+        for (int i = 0; i < 4; ++i) mbar_init(bar_f + 8 * i, 1);
         fence_mbar_init();
     }
     if (tid == kTcThreads) {
@@ -702,7 +706,7 @@ __global__ void __launch_bounds__(kWsThreads, 2)
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::kOffSlot);
     bool ok = true;
 
-    if (warp == kTcThreads / 32) {
+    if (warp == kCopyWarp) {
         // ======================================================== copy warp
         int blk = tma_block_of(p, 0, c, kv_end);
         for (int kt = 0; kt < nkt; ++kt) {
@@ -717,6 +721,7 @@ __global__ void __launch_bounds__(kWsThreads, 2)
             const bool any_hole = __any_sync(0xffffffffu, hole);
             if ((tid & 31) == 0) hflag[kt & 3] = any_hole ? 1 : 0;
             __syncwarp();  // flags stored before lane 0's arrive (release) below
+            if ((tid & 31) == 0) mbar_arrive(bar_f + 8 * (kt & 3));
             issue_kv_ws<D>(p, &tm_k, sbase + L::kOffK + b * L::kKV, bar_k + 8 * b, kt, kvh, blk);
             // V buffer b is free once P V of tile kt - 2 is done
             if (kt >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(bar_o + 8 * b, prev)))
@@ -724,6 +729,50 @@ __global__ void __launch_bounds__(kWsThreads, 2)
             issue_kv_ws<D>(p, &tm_v, sbase + L::kOffV + b * L::kKV, bar_v + 8 * b, kt, kvh, blk);
             blk = blk_next;
         }
+    } else if (warp == kMmaWarp) {
+        // ========================================================= MMA warp
+        if (tid == kMmaWarp * 32) {
+            // S = Q K^T of tile j (M 128, N 64, K = head dim) into S buffer
+            // j % 2, once K of tile j has landed
+            auto issue_s = [&](int j) {
+                const int b = j & 1;
+                if (!mbar_wait_bounded(bar_k + 8 * b, (uint32_t)((j >> 1) & 1))) ok = false;
+                tc5::fence_after_sync();
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    const uint32_t qo = (uint32_t)((ks >> 2) * kTcBQ * 128 + (ks & 3) * 32);
+                    const uint32_t ko = (uint32_t)(b * L::kKV + (ks >> 2) * 1024 + (ks & 3) * 32);
+                    tc5::mma(tmem + b * kTcBK, tc5::desc_sw128(sbase + L::kOffQ + qo, 16, 1024),
+                             tc5::desc_sw128(sbase + L::kOffK + ko, 16, kGroupStride), kIdescS,
+                             ks > 0);
+                }
+                tc5::commit(bar_s + 8 * b);
+            };
+            for (int j = 0; j < min(2, nkt); ++j) issue_s(j);
+            for (int kt = 0; kt < nkt; ++kt) {
+                const int b = kt & 1;
+                const uint32_t par = (uint32_t)((kt >> 1) & 1);
+                // ---- O += P V (M 128, N = head dim, K 64 tokens; P from tensor
+                // memory, V MN-major from shared memory), once every softmax
+                // warp has put P (kt) in place and V (kt) has landed
+                if (!mbar_wait_bounded(bar_p + 8 * b, par)) ok = false;
+                if (!mbar_wait_bounded(bar_v + 8 * b, par)) ok = false;
+                tc5::fence_after_sync();
+#pragma unroll
+                for (int ks = 0; ks < kTcBK / 16; ++ks) {
+                    const uint64_t bdesc = tc5::desc_sw128(
+                        sbase + L::kOffV + b * L::kKV + ks * 2 * kGroupStride, 1024, kGroupStride);
+                    tc5::mma_ts(tmem + 2 * kTcBK, tmem + b * kTcBK + ks * 8, bdesc, kIdescO,
+                                kt > 0 || ks > 0);
+                    if constexpr (kSplit)
+                        tc5::mma_ts(tmem + 2 * kTcBK, tmem + b * kTcBK + 32 + ks * 8, bdesc,
+                                    kIdescO, true);
+                }
+                tc5::commit(bar_o + 8 * b);
+                if (kt + 2 < nkt) issue_s(kt + 2);
+            }
+        }
+        __syncwarp();
     } else {
         // ===================================================== softmax warps
         const uint32_t t_o = tmem + 2 * kTcBK;                   // columns of O
@@ -732,32 +781,11 @@ __global__ void __launch_bounds__(kWsThreads, 2)
         const int qpos = first_pos + tile * kTcBQ + row;
         const float sl2 = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;
-        // S = Q K^T of tile j (M 128, N 64, K = head dim) into S buffer j % 2,
-        // once K of tile j has landed (thread 0)
-        auto issue_s = [&](int j) {
-            const int b = j & 1;
-            if (!mbar_wait_bounded(bar_k + 8 * b, (uint32_t)((j >> 1) & 1))) ok = false;
-            tc5::fence_after_sync();
-#pragma unroll
-            for (int ks = 0; ks < D / 16; ++ks) {
-                const uint32_t qo = (uint32_t)((ks >> 2) * kTcBQ * 128 + (ks & 3) * 32);
-                const uint32_t ko = (uint32_t)(b * L::kKV + (ks >> 2) * 1024 + (ks & 3) * 32);
-                tc5::mma(tmem + b * kTcBK, tc5::desc_sw128(sbase + L::kOffQ + qo, 16, 1024),
-                         tc5::desc_sw128(sbase + L::kOffK + ko, 16, kGroupStride), kIdescS,
-                         ks > 0);
-            }
-            tc5::commit(bar_s + 8 * b);
-        };
-        if (tid == 0) {
-            for (int j = 0; j < min(2, nkt); ++j) issue_s(j);
-        }
-        // thread 0 has seen K of tiles 0 and 1 land: their flags are visible
-        // to every softmax thread past this barrier (and those of tile kt + 2,
-        // seen at the end of iteration kt, past the barrier of iteration kt + 1)
-        softmax_warps_sync();
         for (int kt = 0; kt < nkt; ++kt) {
             const int b = kt & 1;
             const uint32_t par = (uint32_t)((kt >> 1) & 1);  // phase of tile kt on buffer b
+            // the tile's flags are stored, and S of it is done
+            if (!mbar_wait_bounded(bar_f + 8 * (kt & 3), (uint32_t)((kt >> 2) & 1))) ok = false;
             const bool holes = hflag[kt & 3] != 0;
             const uint8_t* okf = smem + L::kOffOk + (kt & 3) * kTcBK;
             if (!mbar_wait_bounded(bar_s + 8 * b, par)) ok = false;
@@ -782,11 +810,10 @@ __global__ void __launch_bounds__(kWsThreads, 2)
             }
             // A box moves whole blocks: V rows past the context, or of an
             // unmapped block (never copied: stale shared memory), are zeroed
-            // once the tile's V has landed, so 0 x (stale NaN) never reaches O.
-            bool v_waited = false;
+            // once the tile's V has landed, so 0 x (stale NaN) never reaches O;
+            // each warp zeroes its own quarter of the rows.
             if (holes || (kt == nkt - 1 && kv_end - kt * kTcBK < kTcBK)) {
                 if (!mbar_wait_bounded(bar_v + 8 * b, par)) ok = false;
-                v_waited = true;
                 for (int i = tid; i < kTcBK * kCh * 8; i += kTcThreads) {
                     const int r = i / (kCh * 8), u = i % (kCh * 8);
                     if (!okf[r])
@@ -797,26 +824,10 @@ __global__ void __launch_bounds__(kWsThreads, 2)
                 }
                 fence_proxy_async_smem();
             }
+            // P (and any zeroed V rows) in place: the warp's arrival releases them
             tc5::fence_before_sync();
-            softmax_warps_sync();
-            tc5::fence_after_sync();
-            if (tid == 0) {
-                // ---- O += P V (M 128, N = head dim, K 64 tokens; P from tensor
-                // memory, V MN-major from shared memory)
-                if (!v_waited && !mbar_wait_bounded(bar_v + 8 * b, par)) ok = false;
-                tc5::fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < kTcBK / 16; ++ks) {
-                    const uint64_t bdesc = tc5::desc_sw128(
-                        sbase + L::kOffV + b * L::kKV + ks * 2 * kGroupStride, 1024, kGroupStride);
-                    tc5::mma_ts(t_o, tmem + b * kTcBK + ks * 8, bdesc, kIdescO, kt > 0 || ks > 0);
-                    if constexpr (kSplit)
-                        tc5::mma_ts(t_o, tmem + b * kTcBK + 32 + ks * 8, bdesc, kIdescO, true);
-                }
-                tc5::commit(bar_o + 8 * b);
-                if (kt + 2 < nkt) issue_s(kt + 2);
-            }
             __syncwarp();
+            if ((tid & 31) == 0) mbar_arrive(bar_p + 8 * b);
         }
         // ---- normalise and store (rows of the chunk only; an empty softmax -> 0)
         T* out = reinterpret_cast<T*>(p.out);
