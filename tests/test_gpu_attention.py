@@ -19,6 +19,21 @@ pytestmark = pytest.mark.gpu
 ATTN_CASES = sorted(glob.glob(str(GOLDEN / "attn_ref_test_*.npz")))
 
 
+def _long_tail_shard():
+    """The long-tail batch's 4-GPU shard that holds its 10295-token sequence
+    (31 sequences): each of that sequence's two units is cut into 81 pieces."""
+    from paged_decode import partition as Pn
+
+    lens = W.long_tail_lengths(0, 256)
+    for shard in Pn.lpt_assign(lens, 4):
+        if max(lens[i] for i in shard) == max(lens):
+            return [lens[i] for i in shard]
+    raise AssertionError("no shard holds the longest sequence")
+
+
+LONG_TAIL_SHARD = _long_tail_shard()
+
+
 def _attend(batch, query=None):
     q = batch.query[batch.decode_rows] if query is None else query
     return A.paged_attention(q.contiguous(), batch.key_cache, batch.value_cache,
@@ -223,6 +238,8 @@ def test_cpu_tensor_raises_reference_message():
     (14, 2, 64, 16, [1, 2, 15, 16, 17, 100, 333, 1024, 0, 77]),
     (16, 1, 128, 64, [4096, 3, 700]),
     (32, 2, 128, 32, [8192, 9, 2000]),             # two head tiles (group 16)
+    (16, 2, 128, 32, LONG_TAIL_SHARD),             # 81 pieces: staged in chunks
+    (8, 1, 128, 32, [32768] + [32] * 300),        # 128 pieces: the epilogue warp merges
 ])
 def test_counters_are_zero_after_every_launch(H, KVH, D, bs, lens, built_lib):
     """Split pieces meet on per-(sequence, kv head) arrival counters that every
@@ -240,7 +257,9 @@ def test_counters_are_zero_after_every_launch(H, KVH, D, bs, lens, built_lib):
 @pytest.mark.parametrize("lens,H,KVH,D", [
     ("qwen3b", 16, 2, 128),                 # the 3B decode batch: many two- to five-piece splits
     ([8192, 8192, 300, 5000], 14, 2, 64),   # head dim 64, units cut into 8+ pieces
-    ([20000], 16, 2, 128),                  # more pieces than the consumer warps merge
+    ([20000], 16, 2, 128),                  # 16 pieces, one staged chunk
+    (LONG_TAIL_SHARD, 16, 2, 128),          # 81 pieces, staged in six chunks
+    ([32768] + [32] * 300, 8, 1, 128),      # 128 pieces: more than the consumer warps merge
 ])
 def test_split_merges_give_the_same_bits_every_launch(lens, H, KVH, D, built_lib):
     """Which piece of a split (sequence, kv head) finishes last changes from

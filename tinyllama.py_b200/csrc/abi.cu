@@ -437,6 +437,9 @@ int attention_impl(void* out, const void* query, const void* key_cache,
         p.min_tokens = TLB_ATTN_MIN_TOKENS;
         p.scale_log2 = scale_log2;
         p.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+        // the caches (the fused step stores the new rows there)
+        p.key_cache = const_cast<void*>(key_cache);
+        p.value_cache = const_cast<void*>(value_cache);
         if (fr != nullptr) {
             p.cos_sin = fr->cos_sin;
             p.cache_rows = fr->cache_rows;
@@ -444,8 +447,6 @@ int attention_impl(void* out, const void* query, const void* key_cache,
             p.value_new = fr->value;
             p.key_stride = fr->key_stride;
             p.value_stride = fr->value_stride;
-            p.key_cache = const_cast<void*>(key_cache);
-            p.value_cache = const_cast<void*>(value_cache);
         }
         e = tlb::attn::launch_tc(dtype, (int)head_dim, group, p, tk, tv, grid,
                                  (flags & TLB_ATTN_OVERLAP_PROLOGUE) != 0, st);

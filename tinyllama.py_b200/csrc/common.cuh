@@ -317,6 +317,12 @@ __device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
                  "l"(reinterpret_cast<uint64_t>(src))
                  : "memory");
 }
+// 16 bytes global -> shared, through L2 only (both addresses 16-byte aligned)
+__device__ __forceinline__ void cp_async_cg16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src))
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;" ::: "memory");
 }

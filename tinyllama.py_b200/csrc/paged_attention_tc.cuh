@@ -145,9 +145,9 @@ __device__ __forceinline__ void add_pair(float4& a, float w0, const float4& v0, 
     a.w = __fadd_rn(a.w, __fmaf_rn(w1, v1.w, __fmul_rn(w0, v0.w)));
 }
 // Most pieces the consumer warps merge themselves (the (m, l) of every piece
-// sit in the hand-off buffer meanwhile); a unit cut into more goes to the
-// epilogue warp.
-constexpr int kConsumerMergeMax = 64;
+// sit in the hand-off buffer meanwhile, which bounds the count); a unit cut
+// into more goes to the epilogue warp.
+constexpr int kConsumerMergeMax = 120;
 // With head dim 64 a piece's partial is half as large and the epilogue
 // warp's merge correspondingly quicker: there the consumer warps take a
 // CTA's last piece only when its unit is cut into at least this many pieces
@@ -1226,10 +1226,14 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             if (!csync()) return;
             if (*sDecide == 0) return;
         }
-        // Merge all n pieces. The first partials are requested first (this
-        // piece's own from registers), then the pieces' (m, l) go through the
-        // hand-off buffer into per-head weights, then every thread sums its
-        // groups over the pieces in pairs, ascending.
+        // Merge all n pieces. The other pieces' partials are staged into the
+        // CTA's K and V stage buffers, free now (the producer has issued its
+        // last copy and every stage has been consumed), with 16-byte cp.async
+        // copies, kStageP pieces per round trip; each thread copies exactly
+        // the float4 groups it sums, so it needs only its own copies to land.
+        // Meanwhile the pieces' (m, l) go through the hand-off buffer into
+        // per-head weights. Every thread then sums its groups over the pieces
+        // in pairs, ascending (this piece's own partial from registers).
         int own = -1;
         if (own_regs)
             for (int k = 0; k < n; ++k)
@@ -1237,21 +1241,29 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         float* sMW = sO;                // [n][GP] maxima, then weights
         float* sML = sMW + n * GP;      // [n][GP] sums
         float* sFL = sML + n * GP;      // [GP] 1 / total
-        constexpr int kBatch = 4;                        // pieces in flight per group and thread
-        constexpr int kPre = kGroups <= 2 ? kBatch : 0;  // the first batch, prefetched
-        float4 vpre[kGroups][kPre > 0 ? kPre : 1];
-        auto piece = [&](int k, int j) -> float4 {
-            const int el = 4 * (tid + NC * j);
-            if (k >= n) return make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k == own) return a[j];
-            return __ldcg(reinterpret_cast<const float4*>(p.ws_o + slot_k(k) * GP * D + el));
+        static_assert(2 * kConsumerMergeMax * GP + GP <= L::kOFloats,
+                      "the weights of every piece fit the hand-off buffer");
+        constexpr int kPieceF = GP * D;  // floats of one partial
+        constexpr int kStageP = (2 * NSTAGE * L::kStageKV) / (kPieceF * 4) / 2 * 2;  // even
+        static_assert(kStageP >= 2 && L::kOffK == 0 && L::kOffV == NSTAGE * L::kStageKV,
+                      "the K and V stage buffers are one run of kStageP partials");
+        const uint32_t sPart = sbase + L::kOffK;
+        auto stage_chunk = [&](int c0) {
+            const int cn = min(kStageP, n - c0);
+            for (int kk = 0; kk < cn; ++kk) {
+                const int k = c0 + kk;
+                if (k == own) continue;
+                const float* src = p.ws_o + slot_k(k) * kPieceF;
+#pragma unroll
+                for (int j = 0; j < kGroups; ++j) {
+                    const int el = 4 * (tid + NC * j);
+                    if (el / D < G)
+                        cp_async_cg16(sPart + (uint32_t)(kk * kPieceF + el) * 4u, src + el);
+                }
+            }
+            cp_async_commit();
         };
-        if constexpr (kPre > 0) {
-#pragma unroll
-            for (int j = 0; j < kGroups; ++j)
-#pragma unroll
-                for (int q = 0; q < kPre; ++q) vpre[j][q] = piece(q, j);
-        }
+        stage_chunk(0);
         for (int idx = tid; idx < n * G; idx += NC) {
             const int k = idx / G, h = idx - (idx / G) * G;
             if (k == own) continue;  // written below by the thread that holds it
@@ -1264,37 +1276,45 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             sMW[own * GP + tid] = hm;
             sML[own * GP + tid] = hl;
         }
-        if (!csync()) return;
+        // A failed phase still waits for this thread's copies: the stage
+        // buffers must not be written once the CTA has left.
+        if (!csync()) { cp_async_wait<0>(); return; }
         if (tid < G) {
             float M = -INFINITY;
             for (int k = 0; k < n; ++k) M = fmaxf(M, sMW[k * GP + tid]);
             const float lt = piece_weights(sMW + tid, sML + tid, n, GP, M, 0.f);
             sFL[tid] = lt > 0.f ? 1.f / lt : 0.f;
         }
-        if (!csync()) return;
+        if (!csync()) { cp_async_wait<0>(); return; }
+        float4 acc[kGroups];
+#pragma unroll
+        for (int j = 0; j < kGroups; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float* sPartF = reinterpret_cast<const float*>(smem + L::kOffK);
+        for (int c0 = 0; c0 < n; c0 += kStageP) {
+            cp_async_wait<0>();  // this thread's copies of the chunk
+            const int cn = min(kStageP, n - c0);
+#pragma unroll
+            for (int j = 0; j < kGroups; ++j) {
+                const int el = 4 * (tid + NC * j), h = el / D;
+                if (h >= G) continue;
+                auto piece = [&](int kk) -> float4 {
+                    if (kk >= cn) return make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (c0 + kk == own) return a[j];
+                    return *reinterpret_cast<const float4*>(sPartF + kk * kPieceF + el);
+                };
+                for (int kk = 0; kk < cn; kk += 2) {
+                    const int k = c0 + kk;
+                    add_pair(acc[j], sMW[k * GP + h], piece(kk),
+                             k + 1 < n ? sMW[(k + 1) * GP + h] : 0.f, piece(kk + 1));
+                }
+            }
+            // the next chunk overwrites only this thread's own groups
+            if (c0 + kStageP < n) stage_chunk(c0 + kStageP);
+        }
 #pragma unroll
         for (int j = 0; j < kGroups; ++j) {
             const int el = 4 * (tid + NC * j), h = el / D;
-            if (h >= G) continue;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k0 = 0; k0 < n; k0 += kBatch) {
-                float4 v[kBatch];
-#pragma unroll
-                for (int q = 0; q < kBatch; ++q) {
-                    if constexpr (kPre > 0)
-                        v[q] = k0 == 0 ? vpre[j][q] : piece(k0 + q, j);
-                    else
-                        v[q] = piece(k0 + q, j);
-                }
-#pragma unroll
-                for (int q = 0; q < kBatch; q += 2) {
-                    const int k = k0 + q;
-                    if (k < n)
-                        add_pair(acc, sMW[k * GP + h], v[q], k + 1 < n ? sMW[(k + 1) * GP + h] : 0.f,
-                                 v[q + 1]);
-                }
-            }
-            Vec4Out<T>::store(out + out_base + el, acc, sFL[h]);
+            if (h < G) Vec4Out<T>::store(out + out_base + el, acc[j], sFL[h]);
         }
     };
 
