@@ -257,7 +257,7 @@ def test_counters_are_zero_after_every_launch(H, KVH, D, bs, lens, built_lib):
 @pytest.mark.parametrize("lens,H,KVH,D", [
     ("qwen3b", 16, 2, 128),                 # the 3B decode batch: many two- to five-piece splits
     ([8192, 8192, 300, 5000], 14, 2, 64),   # head dim 64, units cut into 8+ pieces
-    ([20000], 16, 2, 128),                  # 16 pieces, one staged chunk
+    ([20000], 16, 2, 128),                  # 32 pieces, two staged chunks
     (LONG_TAIL_SHARD, 16, 2, 128),          # 81 pieces, staged in six chunks
     ([32768] + [32] * 300, 8, 1, 128),      # 128 pieces: more than the consumer warps merge
 ])

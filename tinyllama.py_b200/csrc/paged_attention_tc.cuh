@@ -82,7 +82,7 @@ constexpr int kItemCache = 512; // range starts kept in shared memory (grids up 
 // unit's start; a range owns the stages whose cost point lies inside it.
 constexpr int kCostStage = 4;
 #ifndef TLB_ATTN_MAX_SPLITS
-#define TLB_ATTN_MAX_SPLITS 16
+#define TLB_ATTN_MAX_SPLITS 32
 #endif
 constexpr int kMaxSplits = TLB_ATTN_MAX_SPLITS;  // most pieces a (sequence, kv head) is cut into
 constexpr int kCostPiece = 5;
