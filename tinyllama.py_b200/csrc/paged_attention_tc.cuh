@@ -756,7 +756,6 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         // Everything above reads only metadata; the query and the cache may
         // still be written by the kernel launched just before this one.
         grid_dependency_wait();
-        zero_empty_outputs(lane, 32);
         while (nf < 2) prefetch(nf++);
         bool ok = true;
         for (int k = 0;; ++k) {
@@ -765,9 +764,11 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             const Job job = sJob[k % kJobRing];
             if (!job.valid) break;
 
-            bool waited = true;
-            if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, wlim);
-            waited = __shfl_sync(0xffffffffu, waited, 0);
+            bool waited = true;  // the first NSTAGE slots are fresh: no wait
+            if (k >= NSTAGE) {
+                if (lane == 0) waited = mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, wlim);
+                waited = __shfl_sync(0xffffffffu, waited, 0);
+            }
             if (!waited) {
                 if (lane == 0) flag_status(TLB_STATUS_WAIT_TIMEOUT);
                 ok = false;
@@ -799,6 +800,9 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             for (int t = 0; t < 2 && nf < k + 1 + kPrefetch; ++t) prefetch(nf++);
         }
         cp_async_wait<0>();
+        // outputs of sequences with no context (after the stream: they are
+        // not on the way to the first copy)
+        zero_empty_outputs(lane, 32);
         if (T_tail > 0 && lane == 0) {
             // The last CTA to finish taking tail chunks resets the counters
             // for the next launch (they live in the zeroed workspace prefix).
