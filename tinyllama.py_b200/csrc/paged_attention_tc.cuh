@@ -225,13 +225,21 @@ __device__ __forceinline__ long long block_incl_scan(long long v, long long* war
     return v + before;
 }
 
+// Quotient of non-negative a and positive b: one 32-bit division when both
+// fit in 32 bits (every launch below 2^32 cost units), else the 64-bit one.
+__device__ __forceinline__ long long div_nn(long long a, long long b) {
+    return ((unsigned long long)(a | b) >> 32) == 0ull
+               ? (long long)((unsigned)a / (unsigned)b)
+               : a / b;
+}
 // CTA whose unit range [floor(j W / P), floor((j+1) W / P)) contains unit x.
 __device__ __forceinline__ int cta_of(long long x, long long W, int P) {
-    return (int)(((x + 1) * (long long)P - 1) / W);
+    return (int)div_nn((x + 1) * (long long)P - 1, W);
 }
 __device__ __forceinline__ long long range_start(int j, long long W, int P) {
-    return (long long)j * W / P;
+    return div_nn((long long)j * W, P);
 }
+__host__ __device__ constexpr int ilog2_c(int v) { return v <= 1 ? 0 : 1 + ilog2_c(v >> 1); }
 
 
 
@@ -284,6 +292,10 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     const int G = p.group;
     const int bs = p.block_size;
     const int cap_tokens = p.max_blocks * bs;
+    // Block sizes are powers of two (8 to 64; the host checks), so every
+    // division by the block size or by the blocks per stage is a shift.
+    const int bs_sh = __ffs(bs) - 1;
+    static_assert((ROWS & (ROWS - 1)) == 0, "stage rows are a power of two");
 
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; ++i) {
@@ -313,10 +325,12 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     auto len_of = [&](int s) -> int { return s < kSeqCache ? sSeqLen[s] : p.seq_lens[s]; };
     auto blocks_of = [&](int len) -> int {
         len = min(len, cap_tokens);
-        return len > 0 ? (len + bs - 1) / bs : 0;
+        return len > 0 ? (len + bs - 1) >> bs_sh : 0;
     };
-    const int bps = ROWS / bs;  // KV blocks per stage
-    auto stages_of = [&](int len) -> int { return (blocks_of(len) + bps - 1) / bps; };
+    const int bps = ROWS >> bs_sh;  // KV blocks per stage
+    constexpr int kRowsSh = ilog2_c(ROWS);
+    const int bps_sh = kRowsSh - bs_sh;
+    auto stages_of = [&](int len) -> int { return (blocks_of(len) + bps - 1) >> bps_sh; };
     auto cost_of = [&](int len) -> int {  // per kv head
         const int ns = stages_of(len);
         return ns > 0 ? kCostPiece + kCS * ns : 0;
@@ -377,19 +391,19 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         // Ranges of at least min_tokens, and long enough that a
         // (sequence, kv head) of average cost is cut into at most kMaxSplits
         // pieces: the last piece merges the others one pair at a time.
-        const long long avg_unit = W / ((long long)S * KVH);
+        const long long avg_unit = div_nn(W, (long long)S * KVH);
         // Every range is at least one stage's cost long, so a range inside a
         // unit always holds a stage point and each piece count (nsplits) is
         // exact: ranges are floor(Ws / P) or longer.
         const long long min_cost = max((long long)max(1, p.min_tokens / ROWS) * kCS,
                                        (avg_unit + kMaxSplits - 1) / kMaxSplits);
-        const long long want = Ws / min_cost;
+        const long long want = div_nn(Ws, min_cost);
         if (want < P) P = (int)(want > 0 ? want : 1);
     }
     const long long Wt = W - Ws;
-    long long C = (Wt + 2ll * gridDim.x - 1) / (2ll * gridDim.x);
+    long long C = div_nn(Wt + 2ll * gridDim.x - 1, 2ll * gridDim.x);
     if (C < kCS) C = kCS;  // a chunk holds at least one stage point
-    const int T_tail = (int)((Wt + C - 1) / C);
+    const int T_tail = (int)div_nn(Wt + C - 1, C);
     // Range starts go to shared memory once (one 64-bit division per
     // entry, spread over the block), so the producer's per-piece lookups
     // are loads, not divisions.
@@ -409,7 +423,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         return i < P ? static_start(i + 1) : min(W, Ws + (long long)(i - P + 1) * C);
     };
     auto item_of = [&](long long x) -> int {
-        if (x >= Ws) return P + (int)((x - Ws) / C);
+        if (x >= Ws) return P + (int)div_nn(x - Ws, C);
         if (!items_cached) return cta_of(x, Ws, P);
         // float estimate of floor(x P / Ws), corrected against the table
         int g = (int)((float)x * ((float)P / (float)Ws));
@@ -422,11 +436,23 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
 
     // Sequence holding cost point x and its cost prefix: binary search of the
     // cached prefix, or (uncached) a block-wide scan for the static item.
+    // The largest s with sPre[s] * KVH <= x. The prefix is non-decreasing
+    // from sPre[0] = 0, so the sequences that pass form a prefix: with at
+    // most 64 sequences two warp ballots count them (all 32 lanes call this).
     auto locate_cached = [&](long long x, long long& pre) -> int {
-        int lo = 0, hi = S - 1;  // largest s with sPre[s] * KVH <= x
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if ((long long)sPre[mid] * KVH <= x) lo = mid; else hi = mid - 1;
+        int lo;
+        if (S <= 64) {
+            const unsigned t0 = __ballot_sync(0xffffffffu, lane < S && (long long)sPre[lane] * KVH <= x);
+            const unsigned t1 =
+                __ballot_sync(0xffffffffu, lane + 32 < S && (long long)sPre[lane + 32] * KVH <= x);
+            lo = __popc(t0) + __popc(t1) - 1;
+        } else {
+            lo = 0;
+            int hi = S - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if ((long long)sPre[mid] * KVH <= x) lo = mid; else hi = mid - 1;
+            }
         }
         pre = sPre[lo];
         return lo;
@@ -481,7 +507,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         };
         // Whether the new token's block is among this stage's blocks.
         auto new_token_here = [&](const Job& job) -> bool {
-            const int blk_i = job.pos / bs;
+            const int blk_i = job.pos >> bs_sh;  // used only when pos >= 0
             return job.pos >= 0 && job.pos < cap_tokens && blk_i >= job.cb &&
                    blk_i < job.cb + job.nblk;
         };
@@ -781,12 +807,12 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
             const bool new_tok = carries_new_token(job);
             int new_r = -1, new_row = -1;
             if (new_tok && new_token_here(job)) {
-                const int b = job.pos / bs - job.cb;
+                const int b = (job.pos >> bs_sh) - job.cb;
                 new_r = job.pos - job.cb * bs;
                 int32_t y = 0;
 #pragma unroll
                 for (int bb = 0; bb < kBpsMax; ++bb) y = bb == b ? ys[bb] : y;
-                if ((vmask >> b) & 1u) new_row = y + job.pos % bs;
+                if ((vmask >> b) & 1u) new_row = y + (job.pos & (bs - 1));
             }
             if (elect_one()) {
                 // jobs up to k + kPrefetch are in the ring: an invalid next job
@@ -1054,7 +1080,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
 #pragma unroll
     for (int t = 0; t < TPW; ++t) {
         const int ld_r = (t * CW + warp) * kTileRows + ld_row;
-        ld_off_t[t] = (uint32_t)((ld_r / bs) * (bs * D * 2) + (ld_r % bs) * 128);
+        ld_off_t[t] = (uint32_t)((ld_r >> bs_sh) * (bs * D * 2) + (ld_r & (bs - 1)) * 128);
     }
     const uint32_t chunk_bytes = (uint32_t)(bs * 128);
     const int ld_swz = ld_row & 7;  // bs and tile starts are multiples of 8
@@ -1092,8 +1118,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         const long long grow = (long long)dd.new_row * D;
         // the token's row in the stage: block tile new_r / bs, row rr, with
         // the 128-byte swizzle of the copies on its 16-byte units
-        const int rr = store ? dd.new_r % bs : 0;
-        const int roff = store ? (dd.new_r / bs) * (bs * D * 2) + rr * 128 : 0;
+        const int rr = store ? dd.new_r & (bs - 1) : 0;
+        const int roff = store ? (dd.new_r >> bs_sh) * (bs * D * 2) + rr * 128 : 0;
         auto unit_off = [&](int u) -> int {
             return roff + (u >> 3) * (int)chunk_bytes + (((u & 7) ^ (rr & 7)) << 4);
         };
@@ -1403,8 +1429,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
                     const int k = idx & 7;
                     const int sr = r0 + r;
                     if (!((vmask >> r) & 1u))
-                        *reinterpret_cast<uint4*>(vrow + (sr / bs) * (bs * D * 2) + c * chunk_bytes +
-                                                  (sr % bs) * 128 + k * 16) =
+                        *reinterpret_cast<uint4*>(vrow + (sr >> bs_sh) * (bs * D * 2) + c * chunk_bytes +
+                                                  (sr & (bs - 1)) * 128 + k * 16) =
                             make_uint4(0u, 0u, 0u, 0u);
                 }
                 fence_proxy_async_smem();
