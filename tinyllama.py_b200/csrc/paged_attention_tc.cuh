@@ -74,7 +74,6 @@ struct alignas(16) StageDesc {
 constexpr int kSeqCache = 1024; // context lengths kept in shared memory (first 1024 seqs)
 constexpr int kCombineCap = 512; // (split, head) pairs the shared-memory combine handles
 constexpr int kJobRing = 8;     // producer job ring (jobs generated ahead of issue)
-constexpr int kItemCache = 512; // range starts kept in shared memory (grids up to 512 CTAs)
 // Work is measured in cost units: a stage costs kCostStage, and every
 // (sequence, kv head) carries kCostPiece more for starting a piece (query
 // load, hand-off and merge), so ranges that start many pieces get fewer
@@ -189,15 +188,14 @@ struct TcLayout {
     static constexpr int kOffW = kOffEpi + (int)sizeof(StageDesc);     // merge weights, M, L
     static constexpr int kOffCW = kOffW + (CW * kGP + 2 * kGP) * 4;
     static constexpr int kOffOwn = kOffCW + 2 * kCombineCap * 4;      // combine weights, sums
-    static constexpr int kOffItem = kOffOwn + kGP * D * 4;  // a merging piece's own partial
-    static constexpr int kBytes = kOffItem + (kItemCache + 1) * 8;  // start unit of each range
+    static constexpr int kBytes = kOffOwn + kGP * D * 4;  // a merging piece's own partial
     // TMA destinations sit on 1024-byte swizzle atoms; float4 / 16-byte
     // structures on 16 bytes.
     static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kStageKV % 1024 == 0, "TMA tiles");
     static_assert(kOffQ % 16 == 0 && kQBytes % 16 == 0, "bulk copy of the query");
     static_assert(kOffO % 16 == 0 && kOffDesc % 16 == 0 && kOffEpi % 16 == 0 && kOffW % 16 == 0,
                   "16-byte accesses");
-    static_assert(kOffOwn % 16 == 0 && kOffBar % 8 == 0 && kOffItem % 8 == 0 && kOffProd % 8 == 0,
+    static_assert(kOffOwn % 16 == 0 && kOffBar % 8 == 0 && kOffProd % 8 == 0,
                   "aligned words");
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
@@ -404,18 +402,11 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     long long C = div_nn(Wt + 2ll * gridDim.x - 1, 2ll * gridDim.x);
     if (C < kCS) C = kCS;  // a chunk holds at least one stage point
     const int T_tail = (int)div_nn(Wt + C - 1, C);
-    // Range starts go to shared memory once (one 64-bit division per
-    // entry, spread over the block), so the producer's per-piece lookups
-    // are loads, not divisions.
-    long long* sItem = reinterpret_cast<long long*>(smem + L::kOffItem);
-    const bool items_cached = P <= kItemCache;
-    if (items_cached) {
-        for (int i = tid; i <= P; i += blockDim.x) sItem[i] = range_start(i, Ws, P);
-    }
-    __syncthreads();
-    auto static_start = [&](int i) -> long long {
-        return items_cached ? sItem[i] : range_start(i, Ws, P);
-    };
+    // Range starts and the range holding a cost point are computed where
+    // they are needed, not tabulated: with operands below 2^32 each is one
+    // 32-bit division, cheaper than filling a table of all range starts
+    // before the producer's first lookup.
+    auto static_start = [&](int i) -> long long { return range_start(i, Ws, P); };
     auto item_start = [&](int i) -> long long {
         return i < P ? static_start(i) : Ws + (long long)(i - P) * C;
     };
@@ -424,13 +415,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
     };
     auto item_of = [&](long long x) -> int {
         if (x >= Ws) return P + (int)div_nn(x - Ws, C);
-        if (!items_cached) return cta_of(x, Ws, P);
-        // float estimate of floor(x P / Ws), corrected against the table
-        int g = (int)((float)x * ((float)P / (float)Ws));
-        g = max(0, min(P - 1, g));
-        while (g > 0 && sItem[g] > x) --g;
-        while (g + 1 < P && sItem[g + 1] <= x) ++g;
-        return g;
+        return cta_of(x, Ws, P);
     };
     const int j = blockIdx.x;
 
