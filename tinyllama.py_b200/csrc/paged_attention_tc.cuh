@@ -110,7 +110,7 @@ struct alignas(8) Job {
     int b_lo, b_hi;  // block range of the piece
     int st_hi;       // end of the piece in stages of the sequence
     long long pre;   // stages of all sequences before s
-    // Per piece, computed once when the piece starts (64-bit divisions):
+    // Per piece, computed once when the piece starts (a few divisions):
     int nsplits;     // pieces its (sequence, kv head) is cut into (1 = complete)
     int jfirst;      // first work range holding a piece of it
     int first_slot1; // that range stored its piece in its second slot
@@ -620,8 +620,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, (NT == 1 && CW == 4) ? 2 : 1)
         // there with cp.async, so the dependent global read of the block
         // table never sits between two TMA issues. New jobs are generated
         // right after a stage is issued, while the producer would otherwise
-        // wait for a free stage, so the per-piece bookkeeping (64-bit
-        // divisions) never delays an issue. `pj` is the next job to store; it
+        // wait for a free stage, so the per-piece bookkeeping (divisions
+        // and range lookups) never delays an issue. `pj` is the next job to store; it
         // is advanced lazily, so nothing is taken from the tail counter
         // before griddepcontrol.wait.
         Job pj;
